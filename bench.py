@@ -1,0 +1,495 @@
+#!/usr/bin/env python
+"""Benchmark of the sm_100a paged-KV attention forward.
+
+Headline: configuration C5 (large-batch decode: batch 256, kv lengths log-uniform in
+[1024, 32768], 32 q / 8 kv heads, head_dim 128, block_size 16, a 2^21-block pool per GPU),
+metric = KV bytes read per second (TB/s, every attended K/V byte counted once per kv head).
+With N GPUs (one process per GPU, torchrun) the kv heads are sharded: each rank holds
+8/N kv heads (and their q heads) of every sequence in its own pool; no collective runs in
+the timed region. Total work is fixed, so scaling is "strong".
+
+Per step: one forward call over the whole batch. Inputs are larger than L2 (about
+9.6 GB of K/V per step), so no L2 flush is needed for the headline. C1-C4 (N=1 only)
+are timed one call at a time from a CUDA graph with a 256 MB L2 flush between calls.
+
+``--impl reference`` times the reference's own CPU algorithm (the oracle port of
+``flash_attn_varlen_with_block``) on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "cuda-learn_b200"))
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+METRIC = "decode attn KV-read HBM TB/s (C5 large-batch decode)"
+UNIT = "TB/s"
+L2_BYTES = 126 * 1024 * 1024
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-configs", action="store_true", help="skip the C1-C4 side table")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=None, help="override C5 batch (debug only)")
+    ap.add_argument("--num-blocks", type=int, default=None, help="override C5 pool size (debug only)")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0, help="target CPU baseline sample time")
+    return ap.parse_args()
+
+
+def peaks() -> dict:
+    f = ROOT / "MEASURED_PEAKS.json"
+    if f.exists():
+        d = json.loads(f.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+# --------------------------------------------------------------------------------------
+# clocks
+# --------------------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        loaded = [s for s in sm if s > 0.5 * max(sm)] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------------------
+# distributed plumbing
+# --------------------------------------------------------------------------------------
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}")
+    if world > 1:
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def allreduce_max(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# --------------------------------------------------------------------------------------
+# workloads
+# --------------------------------------------------------------------------------------
+def c5_shard(world: int, rank: int, args):
+    from toy_flash_attn.workloads import baseline_config
+
+    if 8 % world:
+        raise SystemExit("C5 shards its 8 kv heads: --gpus must divide 8")
+    hkv = 8 // world
+    return baseline_config("C5", device="cuda", batch=args.batch, num_blocks=args.num_blocks, kv_heads=hkv,
+                           q_heads=4 * hkv)
+
+
+def call(case, out, lse=None, events=None, num_splits=0):
+    from toy_flash_attn import flash_attention_func as faf
+
+    return faf.flash_attn_varlen_with_block_cu_bf16(
+        case.q, case.k_cache, case.v_cache, case.max_seqlen_q, case.cu_seqlens_q, case.max_seqlen_k,
+        case.seqused_k, case.causal, case.window_size, case.block_table, out, softmax_lse=lse,
+        num_splits=num_splits, main_events=events)
+
+
+def plan_of(case):
+    from toy_flash_attn import flash_attention_func as faf
+
+    return faf.plan(case.q, case.k_cache, case.v_cache, case.cu_seqlens_q, case.seqused_k, case.block_table,
+                    case.max_seqlen_q, case.max_seqlen_k, case.causal, case.window_size)
+
+
+# --------------------------------------------------------------------------------------
+# CPU baseline: the reference's algorithm (oracle port) on a bounded sample
+# --------------------------------------------------------------------------------------
+def cpu_sample(case, target_bytes: int | None, max_seqs: int):
+    """Compacted CPU copy of the first sequences of `case` (only their live blocks)."""
+    from toy_flash_attn.workloads import PagedCase, kv_bytes
+
+    used = case.seqused_k.tolist()
+    bs = case.k_cache.shape[1]
+    hkv, d = case.k_cache.shape[2], case.k_cache.shape[3]
+    n, acc = 0, 0
+    while n < min(len(used), max_seqs):
+        acc += used[n] * hkv * d * 4
+        n += 1
+        if target_bytes is not None and acc >= target_bytes:
+            break
+    need = [(used[b] + bs - 1) // bs for b in range(n)]
+    rows = [case.block_table[b, :need[b]].long() for b in range(n)]
+    ids = torch.cat(rows)
+    k = case.k_cache[ids].cpu()
+    v = case.v_cache[ids].cpu()
+    table = torch.full((n, max(need)), -1, dtype=torch.int32)
+    o = 0
+    for b in range(n):
+        table[b, :need[b]] = torch.arange(o, o + need[b], dtype=torch.int32)
+        o += need[b]
+    cu = case.cu_seqlens_q[: n + 1].cpu()
+    q = case.q[: int(cu[-1])].cpu()
+    sub = PagedCase(case.name + f"[:{n}]", q, k, v, cu, case.seqused_k[:n].cpu(), table, case.max_seqlen_q,
+                    max(used[:n]), case.causal, case.window_size)
+    return sub, kv_bytes(sub)
+
+
+def time_reference_port(sub, reps: int = 1) -> float:
+    from oracle.paged_attention import reference_port
+
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        reference_port(sub.q, sub.k_cache, sub.v_cache, sub.max_seqlen_q, sub.cu_seqlens_q, sub.max_seqlen_k,
+                       sub.seqused_k, sub.causal, sub.window_size, sub.block_table)
+    return (time.perf_counter() - t0) / reps
+
+
+def cpu_baseline(case, seconds: float) -> dict:
+    torch.set_num_threads(os.cpu_count() or 1)
+    probe, probe_bytes = cpu_sample(case, None, 2)
+    time_reference_port(probe)  # warm-up
+    t = time_reference_port(probe)
+    rate = probe_bytes / max(t, 1e-9)
+    sub, sub_bytes = cpu_sample(case, int(rate * seconds), 64)
+    t = time_reference_port(sub)
+    return {
+        "value": sub_bytes / t / 1e12,
+        "unit": UNIT,
+        "cores": torch.get_num_threads(),
+        "kind": "port",
+        "sample": f"first {sub.batch} of {case.batch} sequences ({sub_bytes / 1e9:.2f} GB of K/V, "
+                  f"{t:.1f} s), bf16 math as TOY_FLASH_ATTN_USE=reference",
+        "seconds": t,
+    }
+
+
+# --------------------------------------------------------------------------------------
+# side table: C1-C4 on one GPU, per call from a CUDA graph, L2 flushed between calls
+# --------------------------------------------------------------------------------------
+def time_graph_cold(case, iters: int = 20) -> float:
+    out = torch.empty_like(case.q)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            call(case, out)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        call(case, out)
+    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device="cuda")
+    times = []
+    for i in range(iters + 3):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        if i >= 3:
+            times.append(e0.elapsed_time(e1))
+    return statistics.median(times) * 1e3  # us
+
+
+def side_configs(pk: dict) -> dict:
+    from toy_flash_attn.workloads import baseline_config, kv_bytes, prefill_flops
+
+    res = {}
+    for name in ("C1", "C2", "C3", "C4"):
+        case = baseline_config(name, device="cuda")
+        us = time_graph_cold(case)
+        p = plan_of(case)
+        entry = {"us_per_call": round(us, 2), "kernel": "decode" if p["kernel"] == 0 else "prefill",
+                 "splits": p["max_splits"], "tokens_per_s": round(case.q.shape[0] / (us * 1e-6), 1)}
+        if p["kernel"] == 0:
+            gbs = kv_bytes(case) / (us * 1e-6) / 1e9
+            entry.update({"kv_GBps": round(gbs, 1), "hbm_frac": round(gbs / pk["hbm_gbs"], 4)})
+        else:
+            tf = prefill_flops(case) / (us * 1e-6) / 1e12
+            entry.update({"TFLOPs": round(tf, 2), "tensor_frac": round(tf / pk["bf16_tflops"], 4)})
+        res[name] = entry
+        del case
+        torch.cuda.empty_cache()
+    return res
+
+
+# --------------------------------------------------------------------------------------
+# main arms
+# --------------------------------------------------------------------------------------
+def run_reference(args):
+    """Reference arm: the reference's CPU algorithm (oracle port) on the host cores, rank 0
+    only, each step a bounded sample (the first sequences) of C5."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    torch.set_num_threads(os.cpu_count() or 1)
+    case = _c5_cpu_case(64)
+    per_step = max(0.5, args.cpu_seconds / max(1, args.steps + args.warmup))
+    probe, probe_bytes = cpu_sample(case, None, 1)
+    time_reference_port(probe)
+    rate = probe_bytes / max(time_reference_port(probe), 1e-9)
+    sub, sub_bytes = cpu_sample(case, int(rate * per_step), 64)
+    for _ in range(args.warmup):
+        time_reference_port(sub)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        time_reference_port(sub)
+    dt = (time.perf_counter() - t0) / args.steps
+    value = sub_bytes / dt / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": _config_desc(world),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": f"first {sub.batch} of 256 C5 sequences per step ({sub_bytes / 1e9:.3f} GB K/V), "
+                                   "bf16 math as TOY_FLASH_ATTN_USE=reference"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def _c5_cpu_case(n_seqs: int):
+    """The first `n_seqs` sequences of C5 (same kv lengths as the GPU workload) with a CPU
+    pool holding just their blocks; pool size does not change the reference's work."""
+    from toy_flash_attn.workloads import PagedCase, c5_kv_lengths
+
+    kv = c5_kv_lengths()[:n_seqs]
+    bs = 16
+    need = [(n + bs - 1) // bs for n in kv]
+    g = torch.Generator().manual_seed(1005)
+    q = torch.randn(n_seqs, 32, 128, generator=g).to(torch.bfloat16)
+    k = torch.randn(sum(need), bs, 8, 128, generator=g).to(torch.bfloat16)
+    v = torch.randn(sum(need), bs, 8, 128, generator=g).to(torch.bfloat16)
+    perm = torch.randperm(sum(need), generator=g).to(torch.int32)
+    table = torch.full((n_seqs, max(need)), -1, dtype=torch.int32)
+    o = 0
+    for b, n in enumerate(need):
+        table[b, :n] = perm[o:o + n]
+        o += n
+    return PagedCase("C5-cpu", q, k, v, torch.arange(n_seqs + 1, dtype=torch.int32),
+                     torch.tensor(kv, dtype=torch.int32), table, 1, max(kv), True, None)
+
+
+def _config_desc(world: int) -> dict:
+    return {
+        "workload": "C5 large-batch decode",
+        "batch": 256, "q_heads": 32, "kv_heads": 8, "head_dim": 128, "block_size": 16,
+        "kv_lengths": "log-uniform [1024, 32768], seed 5", "pool_blocks_per_gpu": 1 << 21,
+        "parallelism": f"kv-head shards x{world} (8/{world} kv heads per GPU), no collective in the timed region",
+        "l2": "inputs larger than L2 (~9.6 GB K/V per step); no flush needed",
+    }
+
+
+def run_ours(args):
+    world, rank, local = dist_setup(args.gpus)
+    from toy_flash_attn import flash_attention_func as faf
+    from toy_flash_attn.workloads import kv_bytes
+
+    pk = peaks()
+    case = c5_shard(world, rank, args)
+    torch.cuda.synchronize()
+    kvb_local = kv_bytes(case)
+    kvb_total = kvb_local * world
+    out = torch.empty_like(case.q)
+    p = plan_of(case)
+    launches_per_step = 1 + p["combine"]
+
+    for _ in range(max(args.warmup, 3)):
+        call(case, out)
+    torch.cuda.synchronize()
+    assert faf.read_device_error() == 0
+
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        t_start.record()
+        for i in range(args.steps):
+            call(case, out, events=evs[i])
+        t_end.record()
+        torch.cuda.synchronize()
+    barrier(world)
+    ms_local = t_start.elapsed_time(t_end) / args.steps
+    main_ms_local = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    ms = allreduce_max(ms_local, world)
+    main_ms = allreduce_max(main_ms_local, world)
+    assert faf.read_device_error() == 0
+
+    # end to end through the public API with host buffers: h2d of the step's inputs
+    # (q, block table, lengths) from pinned memory, the call, d2h of the output.
+    host_in = {n: getattr(case, n).cpu().pin_memory() for n in ("q", "block_table", "seqused_k", "cu_seqlens_q")}
+    host_out = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    dev_in = {n: torch.empty_like(getattr(case, n)) for n in host_in}
+    h2d = sum(t.numel() * t.element_size() for t in host_in.values())
+    d2h = host_out.numel() * host_out.element_size()
+
+    def e2e_step():
+        for n, t in host_in.items():
+            dev_in[n].copy_(t, non_blocking=True)
+        faf.flash_attn_varlen_func(dev_in["q"], case.k_cache, case.v_cache, case.max_seqlen_q, dev_in["cu_seqlens_q"],
+                                   case.max_seqlen_k, None, dev_in["seqused_k"], case.causal, case.window_size,
+                                   dev_in["block_table"], out=out)
+        host_out.copy_(out, non_blocking=True)
+
+    for _ in range(max(args.warmup, 3)):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = allreduce_max(e0.elapsed_time(e1) / args.steps, world)
+
+    # verification plumbing: gather every rank's output shard to rank 0 (NCCL), outside timing
+    verify = {"gathered": world == 1}
+    if world > 1:
+        import torch.distributed as dist
+
+        gathered = torch.empty((world,) + tuple(out.shape), dtype=out.dtype, device="cuda")
+        dist.all_gather_into_tensor(gathered, out.contiguous())
+        if rank == 0:
+            full = gathered.permute(1, 0, 2, 3).reshape(out.shape[0], -1, out.shape[2])
+            verify = {"gathered": True, "shape": list(full.shape), "finite": bool(torch.isfinite(full).all())}
+    else:
+        verify["finite"] = bool(torch.isfinite(out).all())
+
+    if rank == 0:
+        value = kvb_total / (ms * 1e-3) / 1e12
+        achieved_gbs = kvb_local / (main_ms * 1e-3) / 1e9
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "us_per_call": ms * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: seeded N(0,1) bf16 q/K/V, random non-identity block tables",
+            "config": _config_desc(world),
+            "kv_bytes_per_step": kvb_total,
+            "tokens_per_s": case.q.shape[0] / (ms * 1e-3),
+            "roofline": {
+                "kernel": "decode_kernel (tfa_decode.cu)", "bound": "hbm", "achieved": achieved_gbs,
+                "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved_gbs / pk["hbm_gbs"],
+                "peak_source": pk["source"], "traffic": None,
+                "note": "achieved = algorithmic K/V bytes per launch / mean CUDA-event duration of the attention "
+                        "kernel alone (tfa_fwd_timed), max over ranks",
+            },
+            "e2e": {"value": kvb_total / (e2e_ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
+                    "api": "toy_flash_attn.flash_attention_func.flash_attn_varlen_func"},
+            "gpu_launches": launches_per_step * args.steps,
+            "plan": p,
+            "clocks": clk.summary(),
+            "verify": verify,
+        }
+        if world == 1 and not args.no_configs:
+            del case
+            torch.cuda.empty_cache()
+            line["configs"] = side_configs(pk)
+            case = c5_shard(world, rank, args)
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(case, args.cpu_seconds)
+        print(json.dumps(line), flush=True)
+    barrier(world)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

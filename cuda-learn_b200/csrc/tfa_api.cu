@@ -1,0 +1,331 @@
+// C ABI of the paged attention forward (declared in include/tfa.h): argument checks,
+// split-KV planning, TMA descriptor encoding and kernel launches. Host code only.
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+
+#include "../../include/tfa.h"
+#include "tfa_common.cuh"
+#include "tma_host.h"
+
+namespace tfa {
+namespace {
+
+constexpr size_t kCtrlBytes = 256;  // workspace control block: sched[2], err
+constexpr int kMaxDevices = 128;
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// device < 0 plans for a B200 (148 SMs) without touching the CUDA runtime.
+constexpr int kB200Sms = 148;
+
+int sm_count(int device) {
+  static int cache[kMaxDevices] = {};
+  if (device < 0) return kB200Sms;
+  if (device >= kMaxDevices) return 0;
+  if (cache[device] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return 0;
+    cache[device] = n;
+  }
+  return cache[device];
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int validate(const tfa_fwd_params* p) {
+  if (!p) return TFA_ERR_NULL_POINTER;
+  if (p->batch < 0 || p->total_q < 0 || p->num_q_heads <= 0 || p->num_kv_heads <= 0 || p->block_size <= 0 ||
+      p->num_blocks <= 0 || p->max_seqlen_q < 0 || p->max_seqlen_k < 0)
+    return TFA_ERR_SHAPE;
+  if (p->window_left < -1 || p->window_right < -1) return TFA_ERR_SHAPE;
+  if (p->head_dim != 64 && p->head_dim != 128) return TFA_ERR_HEAD_DIM;
+  if (p->num_q_heads % p->num_kv_heads != 0) return TFA_ERR_GQA;
+  if (!(p->block_size % 16 == 0 || 16 % p->block_size == 0)) return TFA_ERR_BLOCK_SIZE;
+  if (p->total_q > INT32_MAX / 2 || p->batch > INT32_MAX / 2 || p->num_blocks > INT32_MAX ||
+      p->num_q_heads > 4096 || p->max_seqlen_k > INT32_MAX / 2)
+    return TFA_ERR_SHAPE;
+  if (p->batch == 0 || p->total_q == 0) return TFA_OK;
+  if (!p->q || !p->k || !p->v || !p->out || !p->cu_seqlens_q || !p->seqused_k || !p->block_table)
+    return TFA_ERR_NULL_POINTER;
+  if (p->q_stride[2] != 1 || p->out_stride[2] != 1 || p->k_stride[3] != 1 || p->v_stride[3] != 1)
+    return TFA_ERR_LAYOUT;
+  // 16-byte vector access of q / out rows and TMA global-stride rules for the cache
+  if (!aligned16(p->q) || !aligned16(p->out) || !aligned16(p->k) || !aligned16(p->v)) return TFA_ERR_LAYOUT;
+  for (int i = 0; i < 2; ++i)
+    if ((p->q_stride[i] % 8) != 0 || (p->out_stride[i] % 8) != 0) return TFA_ERR_LAYOUT;
+  for (int i = 0; i < 3; ++i)
+    if ((p->k_stride[i] % 8) != 0 || (p->v_stride[i] % 8) != 0 || p->k_stride[i] <= 0 || p->v_stride[i] <= 0)
+      return TFA_ERR_LAYOUT;
+  return TFA_OK;
+}
+
+struct Plan {
+  int kernel;
+  int rows, q_tiles, max_splits, split_cap, num_items, grid, combine;
+  size_t ws_bytes;
+};
+
+int make_plan(const tfa_fwd_params* p, int device, Plan* pl) {
+  const int64_t G = p->num_q_heads / p->num_kv_heads;
+  const bool decode = p->max_seqlen_q * G <= 16;
+  pl->kernel = decode ? 0 : 1;
+  pl->rows = decode ? 16 : 128;
+  int64_t qt = (p->max_seqlen_q * G + pl->rows - 1) / pl->rows;
+  if (qt < 1) qt = 1;
+  pl->q_tiles = (int)qt;
+  // kv span one q tile can attend to
+  int64_t span = p->max_seqlen_k;
+  const int64_t wr_eff = p->causal ? 0 : p->window_right;
+  if (p->window_left >= 0 && wr_eff >= 0) {
+    const int64_t toks = (pl->rows + G - 1) / G + 1;
+    const int64_t w = toks + p->window_left + wr_eff + 1;
+    if (w < span) span = w;
+  }
+  int64_t tiles = span > 0 ? (span + kBN - 1) / kBN + 1 : 1;
+  const int64_t tiles_k = (p->max_seqlen_k + kBN - 1) / kBN;
+  if (tiles > tiles_k) tiles = tiles_k > 0 ? tiles_k : 1;
+  const int sms = sm_count(device);
+  if (sms <= 0) return TFA_ERR_CUDA;
+  int64_t cap, S;
+  if (p->num_splits > 0) {
+    S = p->num_splits < tiles ? p->num_splits : tiles;
+    cap = (tiles + S - 1) / S;
+  } else {
+    const int64_t est = (int64_t)p->batch * p->num_kv_heads * pl->q_tiles * tiles;
+    cap = (est + 2 * sms - 1) / (2 * sms);
+    if (cap < 1) cap = 1;
+    if (cap > 64) cap = 64;
+    S = (tiles + cap - 1) / cap;
+  }
+  if (S < 1) S = 1;
+  pl->max_splits = (int)S;
+  pl->split_cap = (int)cap;
+  const int64_t items = S * pl->q_tiles * p->batch * p->num_kv_heads;
+  if (items > INT32_MAX / 2) return TFA_ERR_SHAPE;
+  pl->num_items = (int)items;
+  pl->grid = (int)(items < sms ? items : sms);
+  if (pl->grid < 1) pl->grid = 1;
+  pl->combine = S > 1 ? 1 : 0;
+  size_t ws = kCtrlBytes;
+  if (S > 1) {
+    const size_t rows = (size_t)S * p->total_q * p->num_q_heads;
+    ws += align_up(rows * sizeof(float), 256);
+    ws += rows * p->head_dim * sizeof(float);
+  }
+  pl->ws_bytes = ws;
+  return TFA_OK;
+}
+
+int current_device(int* dev) {
+  if (cudaGetDevice(dev) != cudaSuccess) return TFA_ERR_CUDA;
+  return TFA_OK;
+}
+
+void fill_params(const tfa_fwd_params* a, const Plan& pl, void* ws, FwdParams* p) {
+  std::memset(p, 0, sizeof(*p));
+  p->q = reinterpret_cast<const __nv_bfloat16*>(a->q);
+  p->q_s0 = a->q_stride[0];
+  p->q_s1 = a->q_stride[1];
+  p->out = reinterpret_cast<__nv_bfloat16*>(a->out);
+  p->o_s0 = a->out_stride[0];
+  p->o_s1 = a->out_stride[1];
+  p->lse = a->softmax_lse;
+  p->cu_seqlens_q = a->cu_seqlens_q;
+  p->seqused_k = a->seqused_k;
+  p->block_table = a->block_table;
+  p->bt_s0 = a->block_table_stride0;
+  p->batch = (int)a->batch;
+  p->total_q = (int)a->total_q;
+  p->hq = (int)a->num_q_heads;
+  p->hkv = (int)a->num_kv_heads;
+  p->group = (int)(a->num_q_heads / a->num_kv_heads);
+  p->block_size = (int)a->block_size;
+  p->box_rows = a->block_size < 16 ? (int)a->block_size : 16;
+  p->num_blocks = (int)a->num_blocks;
+  p->causal = a->causal ? 1 : 0;
+  p->wl = a->window_left;
+  p->wr = a->window_right;
+  const float scale = a->softmax_scale > 0.f ? a->softmax_scale : 1.0f / std::sqrt((float)a->head_dim);
+  p->scale_log2 = scale * 1.4426950408889634f;
+  p->rows_per_tile = pl.rows;
+  p->q_tiles = pl.q_tiles;
+  p->max_splits = pl.max_splits;
+  p->split_cap = pl.split_cap;
+  p->num_items = pl.num_items;
+  uint8_t* w = reinterpret_cast<uint8_t*>(ws);
+  p->sched = reinterpret_cast<int*>(w);
+  p->err = reinterpret_cast<int*>(w) + 2;
+  if (pl.max_splits > 1) {
+    const size_t rows = (size_t)pl.max_splits * a->total_q * a->num_q_heads;
+    p->split_lse = reinterpret_cast<float*>(w + kCtrlBytes);
+    p->split_o = reinterpret_cast<float*>(w + kCtrlBytes + align_up(rows * sizeof(float), 256));
+  }
+}
+
+int encode_maps(const tfa_fwd_params* a, int box_rows, KvMaps* m) {
+  const int64_t ks[3] = {a->k_stride[0], a->k_stride[1], a->k_stride[2]};
+  const int64_t vs[3] = {a->v_stride[0], a->v_stride[1], a->v_stride[2]};
+  if (encode_kv_map(&m->k_box, a->k, a->num_blocks, a->block_size, a->num_kv_heads, a->head_dim, ks, box_rows) ||
+      encode_kv_map(&m->k_row, a->k, a->num_blocks, a->block_size, a->num_kv_heads, a->head_dim, ks, 1) ||
+      encode_kv_map(&m->v_box, a->v, a->num_blocks, a->block_size, a->num_kv_heads, a->head_dim, vs, box_rows) ||
+      encode_kv_map(&m->v_row, a->v, a->num_blocks, a->block_size, a->num_kv_heads, a->head_dim, vs, 1))
+    return TFA_ERR_TENSOR_MAP;
+  return TFA_OK;
+}
+
+int check_device(int dev) {
+  static int cc_major[kMaxDevices] = {};
+  if (dev < 0 || dev >= kMaxDevices) return TFA_ERR_DEVICE;
+  if (cc_major[dev] == 0) {
+    int major = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return TFA_ERR_CUDA;
+    cc_major[dev] = major;
+  }
+  return cc_major[dev] == 10 ? TFA_OK : TFA_ERR_DEVICE;
+}
+
+}  // namespace
+}  // namespace tfa
+
+using namespace tfa;
+
+extern "C" {
+
+int tfa_device_sm_count(int device) { return sm_count(device); }
+
+const char* tfa_status_string(int s) {
+  switch (s) {
+    case TFA_OK: return "ok";
+    case TFA_ERR_NULL_POINTER: return "a required pointer is NULL";
+    case TFA_ERR_HEAD_DIM: return "head_dim must be 64 or 128";
+    case TFA_ERR_GQA: return "num_q_heads must be a multiple of num_kv_heads";
+    case TFA_ERR_BLOCK_SIZE: return "block_size must divide 16 or be a multiple of 16";
+    case TFA_ERR_LAYOUT: return "head_dim must be contiguous and pointers/strides 16-byte aligned";
+    case TFA_ERR_SHAPE: return "invalid sizes or window";
+    case TFA_ERR_WORKSPACE: return "workspace missing or too small";
+    case TFA_ERR_TENSOR_MAP: return "TMA descriptor encoding failed";
+    case TFA_ERR_CUDA: return "CUDA call or launch failed";
+    case TFA_ERR_DEVICE: return "current device is not an sm_100 GPU";
+    case TFA_ERR_KERNEL: return "a kernel reported an error";
+    default: return "unknown status";
+  }
+}
+
+int tfa_plan(const tfa_fwd_params* p, int device, tfa_plan_info* info) {
+  if (!info) return TFA_ERR_NULL_POINTER;
+  int rc = validate(p);
+  if (rc != TFA_OK) return rc;
+  Plan pl;
+  rc = make_plan(p, device, &pl);
+  if (rc != TFA_OK) return rc;
+  info->kernel = pl.kernel;
+  info->rows_per_tile = pl.rows;
+  info->q_tiles = pl.q_tiles;
+  info->max_splits = pl.max_splits;
+  info->split_cap = pl.split_cap;
+  info->num_items = pl.num_items;
+  info->grid = pl.grid;
+  info->combine = pl.combine;
+  info->workspace_bytes = pl.ws_bytes;
+  return TFA_OK;
+}
+
+size_t tfa_workspace_size(const tfa_fwd_params* p, int device) {
+  if (validate(p) != TFA_OK) return 0;
+  Plan pl;
+  if (make_plan(p, device, &pl) != TFA_OK) return 0;
+  return pl.ws_bytes;
+}
+
+namespace {
+int fwd_impl(const tfa_fwd_params* a, void* workspace, size_t workspace_bytes, void* stream, void* ev_begin,
+             void* ev_end) {
+  int rc = validate(a);
+  if (rc != TFA_OK) return rc;
+  if (a->batch == 0 || a->total_q == 0) return TFA_OK;
+  int dev = 0;
+  if ((rc = current_device(&dev)) != TFA_OK) return rc;
+  if ((rc = check_device(dev)) != TFA_OK) return rc;
+  Plan pl;
+  if ((rc = make_plan(a, dev, &pl)) != TFA_OK) return rc;
+  if (!workspace || workspace_bytes < pl.ws_bytes || !aligned16(workspace)) return TFA_ERR_WORKSPACE;
+  FwdParams p;
+  fill_params(a, pl, workspace, &p);
+  KvMaps maps;
+  if ((rc = encode_maps(a, p.box_rows, &maps)) != TFA_OK) return rc;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (ev_begin && cudaEventRecord(reinterpret_cast<cudaEvent_t>(ev_begin), s) != cudaSuccess) return TFA_ERR_CUDA;
+  if (a->head_dim == 64)
+    e = pl.kernel == 0 ? launch_decode<64>(p, maps, pl.grid, s) : launch_prefill<64>(p, maps, pl.grid, s);
+  else
+    e = pl.kernel == 0 ? launch_decode<128>(p, maps, pl.grid, s) : launch_prefill<128>(p, maps, pl.grid, s);
+  if (e != cudaSuccess) return TFA_ERR_CUDA;
+  if (ev_end && cudaEventRecord(reinterpret_cast<cudaEvent_t>(ev_end), s) != cudaSuccess) return TFA_ERR_CUDA;
+  if (pl.combine) {
+    e = a->head_dim == 64 ? launch_combine<64>(p, s) : launch_combine<128>(p, s);
+    if (e != cudaSuccess) return TFA_ERR_CUDA;
+  }
+  return TFA_OK;
+}
+}  // namespace
+
+int tfa_fwd(const tfa_fwd_params* a, void* workspace, size_t workspace_bytes, void* stream) {
+  return fwd_impl(a, workspace, workspace_bytes, stream, nullptr, nullptr);
+}
+
+int tfa_fwd_timed(const tfa_fwd_params* a, void* workspace, size_t workspace_bytes, void* stream, void* main_begin,
+                  void* main_end) {
+  if (!main_begin || !main_end) return TFA_ERR_NULL_POINTER;
+  return fwd_impl(a, workspace, workspace_bytes, stream, main_begin, main_end);
+}
+
+int tfa_read_device_error(void* workspace, void* stream, int* err) {
+  if (!workspace || !err) return TFA_ERR_NULL_POINTER;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int* dev_err = reinterpret_cast<int*>(workspace) + 2;
+  int host = 0;
+  if (cudaMemcpyAsync(&host, dev_err, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess) return TFA_ERR_CUDA;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return TFA_ERR_CUDA;
+  *err = host;
+  if (host != 0) {
+    if (cudaMemsetAsync(dev_err, 0, sizeof(int), s) != cudaSuccess) return TFA_ERR_CUDA;
+    if (cudaStreamSynchronize(s) != cudaSuccess) return TFA_ERR_CUDA;
+  }
+  return TFA_OK;
+}
+
+int tfa_gather_kv(const tfa_fwd_params* a, const int64_t* kv_offsets, void* k_out, void* v_out, void* workspace,
+                  void* stream) {
+  if (!a || !kv_offsets || !k_out || !v_out || !workspace) return TFA_ERR_NULL_POINTER;
+  tfa_fwd_params b = *a;
+  // the gather reads no q / out; give validate() harmless stand-ins
+  b.q = b.out = k_out;
+  b.q_stride[0] = b.out_stride[0] = 8;
+  b.q_stride[1] = b.out_stride[1] = 8;
+  b.q_stride[2] = b.out_stride[2] = 1;
+  if (b.total_q <= 0) b.total_q = 1;
+  int rc = validate(&b);
+  if (rc != TFA_OK) return rc;
+  if (b.batch == 0 || b.max_seqlen_k == 0) return TFA_OK;
+  int dev = 0;
+  if ((rc = current_device(&dev)) != TFA_OK) return rc;
+  if ((rc = check_device(dev)) != TFA_OK) return rc;
+  Plan pl{};
+  pl.rows = 16;
+  pl.q_tiles = 1;
+  pl.max_splits = 1;
+  pl.split_cap = 1;
+  FwdParams p;
+  fill_params(&b, pl, workspace, &p);
+  KvMaps maps;
+  if ((rc = encode_maps(&b, p.box_rows, &maps)) != TFA_OK) return rc;
+  const int max_tiles = (int)((b.max_seqlen_k + kBN - 1) / kBN);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  cudaError_t e = b.head_dim == 64 ? launch_gather<64>(p, maps, max_tiles, kv_offsets, k_out, v_out, s)
+                                   : launch_gather<128>(p, maps, max_tiles, kv_offsets, k_out, v_out, s);
+  return e == cudaSuccess ? TFA_OK : TFA_ERR_CUDA;
+}
+
+}  // extern "C"

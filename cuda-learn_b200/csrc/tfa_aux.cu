@@ -1,0 +1,150 @@
+// LSE combine of split-KV partial outputs, and the gather debug kernel.
+#include <cmath>
+
+#include "tfa_common.cuh"
+
+namespace tfa {
+
+namespace {
+
+// Restates the merge of v8's splitkv_combine_kernel (v8/flash_attn_func.cu:701-777):
+// out = sum_s 2^(lse_s - M) * o_s / sum_s 2^(lse_s - M), M = max_s lse_s, all in the
+// log2 domain of the scaled scores. One warp per (q token, q head); partial outputs are
+// already normalised per split. Only (token, head) pairs whose q tile was split run here;
+// the others were written directly by the attention kernel.
+template <int D>
+__global__ void __launch_bounds__(128) combine_kernel(const __grid_constant__ FwdParams p) {
+  constexpr int EPL = D / 32;  // elements per lane
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t pair = (int64_t)blockIdx.x * 4 + warp;
+  if (pair >= (int64_t)p.total_q * p.hq) return;
+  const int tok = (int)(pair / p.hq), qh = (int)(pair % p.hq);
+  int lo = 0, hi = p.batch - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (__ldg(p.cu_seqlens_q + mid) <= tok) lo = mid;
+    else hi = mid - 1;
+  }
+  const int b = lo;
+  const int q0 = __ldg(p.cu_seqlens_q + b);
+  const int q_len = __ldg(p.cu_seqlens_q + b + 1) - q0;
+  const int kv_len = __ldg(p.seqused_k + b);
+  const int R = (tok - q0) * p.group + qh % p.group;
+  const int row0 = (R / p.rows_per_tile) * p.rows_per_tile;
+  const int nrows = imin(p.rows_per_tile, q_len * p.group - row0);
+  int t_lo, n;
+  tile_span(p, q_len, kv_len, row0, nrows, t_lo, n);
+  const int ns = splits_for(p, n);
+  if (ns <= 1) return;
+
+  const int64_t stride = (int64_t)p.total_q * p.hq;
+  float mx = -INFINITY;
+  for (int s = lane; s < ns; s += 32) mx = fmaxf(mx, p.split_lse[s * stride + pair]);
+  mx = warp_max(mx);
+  __nv_bfloat16* dst = p.out + (int64_t)tok * p.o_s0 + (int64_t)qh * p.o_s1 + lane * EPL;
+  if (mx == -INFINITY) {
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) dst[e] = __float2bfloat16(0.f);
+    if (lane == 0 && p.lse) p.lse[pair] = -INFINITY;
+    return;
+  }
+  float acc[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) acc[e] = 0.f;
+  float wsum = 0.f;
+  for (int s = 0; s < ns; ++s) {
+    const float ls = p.split_lse[s * stride + pair];
+    const float wgt = (ls == -INFINITY) ? 0.f : ex2_approx(ls - mx);
+    wsum += wgt;
+    const float* src = p.split_o + (s * stride + pair) * D + lane * EPL;
+    if constexpr (EPL == 4) {
+      const float4 v = *reinterpret_cast<const float4*>(src);
+      acc[0] += wgt * v.x;
+      acc[1] += wgt * v.y;
+      acc[2] += wgt * v.z;
+      acc[3] += wgt * v.w;
+    } else {
+      const float2 v = *reinterpret_cast<const float2*>(src);
+      acc[0] += wgt * v.x;
+      acc[1] += wgt * v.y;
+    }
+  }
+  const float inv = 1.f / wsum;
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) dst[e] = __float2bfloat16(acc[e] * inv);
+  if (lane == 0 && p.lse) p.lse[pair] = (mx + lg2_approx(wsum)) * kLn2;
+}
+
+// One CTA per (kv tile, sequence, kv head): the producer warp stages the tile with the
+// attention kernels' TMA gather (produce_tile), then all threads copy the valid rows out.
+template <int D>
+__global__ void __launch_bounds__(128) gather_kernel(const __grid_constant__ FwdParams p,
+                                                     const __grid_constant__ KvMaps maps, const int64_t* kv_offsets,
+                                                     __nv_bfloat16* k_out, __nv_bfloat16* v_out) {
+  extern __shared__ uint8_t dyn_smem[];
+  uint8_t* stage = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dyn_smem) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t full;
+  __shared__ volatile int abort_flag;
+  const int t = blockIdx.x, b = blockIdx.y, h = blockIdx.z;
+  const int kv_len = p.seqused_k[b];
+  if (t * kBN >= kv_len) return;
+  if (threadIdx.x == 0) {
+    mbar_init(&full, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  Work w{};
+  w.b = b;
+  w.h = h;
+  w.kv_len = kv_len;
+  if (threadIdx.x < 32) produce_tile<D>(p, maps, w, t, stage, &full, threadIdx.x, l2_policy_evict_first());
+  if (!mbar_wait(&full, 0, &abort_flag, p.err, kDevErrTimeoutProducer)) return;
+  const int rows = imin(kBN, kv_len - t * kBN);
+  const int64_t base = kv_offsets[b] + (int64_t)t * kBN;
+  for (int i = threadIdx.x; i < rows * D; i += blockDim.x) {
+    const int r = i / D, c = i % D;
+    const uint32_t off = sw128_offset(r, c, kBN);
+    const int64_t o = ((base + r) * p.hkv + h) * D + c;
+    v_out[o] = *reinterpret_cast<const __nv_bfloat16*>(stage + off);
+    k_out[o] = *reinterpret_cast<const __nv_bfloat16*>(stage + KvStage<D>::kTensorBytes + off);
+  }
+}
+
+}  // namespace
+
+template <int D>
+cudaError_t launch_combine(const FwdParams& p, cudaStream_t s) {
+  const int64_t pairs = (int64_t)p.total_q * p.hq;
+  const int64_t blocks = (pairs + 3) / 4;
+  combine_kernel<D><<<(unsigned)blocks, 128, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
+template <int D>
+cudaError_t launch_gather(const FwdParams& p, const KvMaps& maps, int max_tiles, const int64_t* kv_offsets,
+                          void* k_out, void* v_out, cudaStream_t s) {
+  const int smem = KvStage<D>::kBytes + 1024;
+  static bool configured[128] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(gather_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  dim3 grid(max_tiles, p.batch, p.hkv);
+  gather_kernel<D><<<grid, 128, smem, s>>>(p, maps, kv_offsets, reinterpret_cast<__nv_bfloat16*>(k_out),
+                                           reinterpret_cast<__nv_bfloat16*>(v_out));
+  return cudaGetLastError();
+}
+
+template cudaError_t launch_combine<64>(const FwdParams&, cudaStream_t);
+template cudaError_t launch_combine<128>(const FwdParams&, cudaStream_t);
+template cudaError_t launch_gather<64>(const FwdParams&, const KvMaps&, int, const int64_t*, void*, void*,
+                                       cudaStream_t);
+template cudaError_t launch_gather<128>(const FwdParams&, const KvMaps&, int, const int64_t*, void*, void*,
+                                        cudaStream_t);
+
+}  // namespace tfa

@@ -1,0 +1,255 @@
+// Shared device code of the paged attention forward: kernel parameters, the work-item
+// decomposition (sequence x kv head x q tile x kv split), the mask rule and the paged
+// K/V producer (TMA gather through block_table).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "sm100.cuh"
+
+namespace tfa {
+
+constexpr int kBN = 128;           // kv tokens per tile
+constexpr float kLn2 = 0.69314718055994530942f;
+
+// Error codes written by kernels into params.err (first one wins).
+enum DeviceError : int {
+  kDevErrTimeoutProducer = 101,
+  kDevErrTimeoutMma = 102,
+  kDevErrTimeoutSoftmax = 103,
+  kDevErrBadBlockId = 110,
+};
+
+struct FwdParams {
+  const __nv_bfloat16* q;  // [total_q, Hq, D], row strides in elements
+  int64_t q_s0, q_s1;
+  __nv_bfloat16* out;      // [total_q, Hq, D]
+  int64_t o_s0, o_s1;
+  float* lse;              // optional [total_q, Hq] natural-log LSE (contiguous)
+  const int* cu_seqlens_q; // [batch + 1]
+  const int* seqused_k;    // [batch]
+  const int* block_table;  // [batch, bt_s0...] (inner stride 1)
+  int64_t bt_s0;
+  int batch, total_q, hq, hkv, group;
+  int block_size, box_rows, num_blocks;
+  int causal, wl, wr;      // window sides, -1 = unbounded
+  float scale_log2;        // softmax_scale * log2(e)
+  int rows_per_tile;       // packed (token, q head) rows per item: 16 (decode) or 128 (prefill)
+  int q_tiles;             // q tiles per (sequence, kv head)
+  int max_splits;          // S_max: split slots per (sequence, kv head, q tile)
+  int split_cap;           // max kv tiles per split
+  int num_items;           // max_splits * q_tiles * batch * hkv
+  float* split_o;          // [max_splits, total_q, Hq, D] fp32 (normalised partial outputs)
+  float* split_lse;        // [max_splits, total_q, Hq] fp32 (log2 domain, scaled)
+  int* sched;              // [2]: next-item counter, finished-CTA counter (self-resetting)
+  int* err;                // first device error code, 0 if none
+};
+
+// One unit of work: the packed q rows [row0, row0 + nrows) of kv head h of sequence b,
+// against kv tiles [tile_begin, tile_end).
+struct Work {
+  int b, h, split, nsplits;
+  int q0, q_len, kv_len;
+  int row0, nrows;
+  int tile_begin, tile_end;
+  bool exists;  // false: split slot unused by this sequence (nothing to do, nothing to write)
+};
+
+__device__ __forceinline__ int imin(int a, int b) { return a < b ? a : b; }
+__device__ __forceinline__ int imax(int a, int b) { return a > b ? a : b; }
+
+// Visible kv range [lo, hi] of query token i (0-based within its sequence).
+// Restates the rule of flash_attention_func.py:367-376 with q/kv tail alignment.
+__device__ __forceinline__ void visible_range(const FwdParams& p, int i, int q_len, int kv_len, int& lo, int& hi) {
+  const int off = kv_len - q_len;
+  lo = p.wl < 0 ? 0 : imax(0, i + off - p.wl);
+  int h = (p.causal || p.wr >= 0) ? (i + off + (p.causal ? 0 : p.wr)) : (kv_len - 1);
+  hi = imin(kv_len - 1, h);
+}
+
+// Number of kv tiles (and the first tile) touched by a q tile, before splitting.
+__device__ __forceinline__ void tile_span(const FwdParams& p, int q_len, int kv_len, int row0, int nrows, int& t_lo,
+                                          int& n_tiles) {
+  n_tiles = 0;
+  t_lo = 0;
+  if (nrows <= 0 || kv_len <= 0) return;
+  int lo_a, hi_a, lo_b, hi_b;
+  visible_range(p, row0 / p.group, q_len, kv_len, lo_a, hi_a);
+  visible_range(p, (row0 + nrows - 1) / p.group, q_len, kv_len, lo_b, hi_b);
+  const int lo = imax(0, lo_a);
+  const int hi = imin(kv_len - 1, hi_b);
+  if (hi < lo) return;
+  t_lo = lo / kBN;
+  n_tiles = hi / kBN - t_lo + 1;
+}
+
+__device__ __forceinline__ int splits_for(const FwdParams& p, int n_tiles) {
+  if (n_tiles <= 0) return 1;
+  return imin(p.max_splits, (n_tiles + p.split_cap - 1) / p.split_cap);
+}
+
+// Item order: split slot slowest, then q tile (longest first for causal prefill),
+// then sequence, then kv head.
+__device__ __forceinline__ Work get_work(const FwdParams& p, int idx) {
+  Work w;
+  w.h = idx % p.hkv;
+  idx /= p.hkv;
+  w.b = idx % p.batch;
+  idx /= p.batch;
+  const int qt = p.q_tiles - 1 - (idx % p.q_tiles);
+  w.split = idx / p.q_tiles;
+  w.q0 = p.cu_seqlens_q[w.b];
+  w.q_len = p.cu_seqlens_q[w.b + 1] - w.q0;
+  w.kv_len = p.seqused_k[w.b];
+  w.row0 = qt * p.rows_per_tile;
+  w.nrows = imax(0, imin(p.rows_per_tile, w.q_len * p.group - w.row0));
+  int t_lo, n;
+  tile_span(p, w.q_len, w.kv_len, w.row0, w.nrows, t_lo, n);
+  w.nsplits = splits_for(p, n);
+  w.exists = w.nrows > 0 && w.split < w.nsplits;
+  w.tile_begin = t_lo + (int)(((long long)n * w.split) / w.nsplits);
+  w.tile_end = t_lo + (int)(((long long)n * (w.split + 1)) / w.nsplits);
+  if (!w.exists) w.tile_end = w.tile_begin;
+  return w;
+}
+
+// ---------------------------------------------------------------------------
+// Paged K/V producer: one warp gathers the 128-token tile of kv head h of sequence b
+// into a pipeline stage laid out as [V panels][K panels], each panel 128 rows x 128 B
+// (64 head-dim columns, 128-byte swizzle). Rows at or past kv_len are zero-filled by
+// out-of-range TMA coordinates, so stale or NaN cache slots never reach an MMA.
+// ---------------------------------------------------------------------------
+template <int D>
+struct KvStage {
+  static constexpr int kPanels = D / 64;
+  static constexpr int kPanelBytes = kBN * 128;            // 16 KB
+  static constexpr int kTensorBytes = kPanels * kPanelBytes;
+  static constexpr int kBytes = 2 * kTensorBytes;          // V then K
+};
+
+struct KvMaps {
+  CUtensorMap k_box, k_row, v_box, v_row;
+};
+
+template <int D>
+__device__ __forceinline__ void produce_tile(const FwdParams& p, const KvMaps& maps, const Work& w, int tile,
+                                             uint8_t* stage, uint64_t* full_bar, int lane, uint64_t policy) {
+  if (lane == 0) mbar_arrive_expect_tx(full_bar, KvStage<D>::kBytes);
+  __syncwarp();
+  const int R = p.box_rows;
+  const int groups = kBN / R;
+  const int bs = p.block_size;
+  const int* bt_row = p.block_table + (int64_t)w.b * p.bt_s0;
+  for (int g = lane; g < groups; g += 32) {
+    const int pos = tile * kBN + g * R;
+    int valid = w.kv_len - pos;
+    valid = valid < 0 ? 0 : (valid > R ? R : valid);
+    int page = p.num_blocks;  // out of range -> zero fill
+    const int slot = pos % bs;
+    if (valid > 0) {
+      page = __ldg(bt_row + pos / bs);
+      if (page < 0 || page >= p.num_blocks) {
+        atomicCAS(p.err, 0, (int)kDevErrBadBlockId);
+        page = p.num_blocks;
+        valid = R;  // whole box out of range -> zeros
+      }
+    }
+    const uint32_t v_dst = smem_u32(stage) + g * R * 128;
+    const uint32_t k_dst = v_dst + KvStage<D>::kTensorBytes;
+#pragma unroll
+    for (int ch = 0; ch < KvStage<D>::kPanels; ++ch) {
+      const uint32_t off = ch * KvStage<D>::kPanelBytes;
+      if (valid == R) {
+        tma_load_4d(k_dst + off, &maps.k_box, ch * 64, w.h, slot, page, full_bar, policy);
+        tma_load_4d(v_dst + off, &maps.v_box, ch * 64, w.h, slot, page, full_bar, policy);
+      } else if (valid == 0) {
+        tma_load_4d(k_dst + off, &maps.k_box, ch * 64, w.h, 0, p.num_blocks, full_bar, policy);
+        tma_load_4d(v_dst + off, &maps.v_box, ch * 64, w.h, 0, p.num_blocks, full_bar, policy);
+      } else {
+        for (int r = 0; r < R; ++r) {
+          const int s = r < valid ? slot + r : bs;  // slot index bs is out of range -> zeros
+          tma_load_4d(k_dst + off + r * 128, &maps.k_row, ch * 64, w.h, s, page, full_bar, policy);
+          tma_load_4d(v_dst + off + r * 128, &maps.v_row, ch * 64, w.h, s, page, full_bar, policy);
+        }
+      }
+    }
+  }
+}
+
+// Producer warp main loop shared by both kernels. Fetches work items dynamically,
+// publishes each into the two-slot item queue and streams their kv tiles.
+template <int D, int STAGES>
+__device__ __forceinline__ void producer_loop(const FwdParams& p, const KvMaps& maps, uint8_t* stages,
+                                              uint64_t* full, uint64_t* empty, uint64_t* item_full,
+                                              uint64_t* item_empty, int* item_slot, volatile int* abort_flag,
+                                              int lane) {
+  const uint64_t policy = l2_policy_evict_first();
+  int c = 0;
+  for (int k = 0;; ++k) {
+    const int slot = k & 1;
+    if (!mbar_wait(&item_empty[slot], ((k >> 1) & 1) ^ 1, abort_flag, p.err, kDevErrTimeoutProducer)) return;
+    int idx = 0;
+    Work w;
+    // Skip split slots a sequence does not use without bothering the consumers.
+    for (;;) {
+      if (lane == 0) idx = atomicAdd(&p.sched[0], 1);
+      idx = __shfl_sync(0xffffffffu, idx, 0);
+      if (idx >= p.num_items) break;
+      w = get_work(p, idx);
+      if (w.exists) break;
+    }
+    if (lane == 0) {
+      item_slot[slot] = idx;
+      mbar_arrive(&item_full[slot]);
+    }
+    if (idx >= p.num_items) return;
+    for (int t = w.tile_begin; t < w.tile_end; ++t, ++c) {
+      const int st = c % STAGES;
+      if (!mbar_wait(&empty[st], ((c / STAGES) & 1) ^ 1, abort_flag, p.err, kDevErrTimeoutProducer)) return;
+      produce_tile<D>(p, maps, w, t, stages + st * KvStage<D>::kBytes, &full[st], lane, policy);
+    }
+  }
+}
+
+// Grid-wide epilogue: the last CTA to finish resets the scheduler counters so the
+// workspace is ready for the next launch on the same stream.
+__device__ __forceinline__ void scheduler_finish(const FwdParams& p) {
+  __threadfence();
+  if (atomicAdd(&p.sched[1], 1) == (int)gridDim.x - 1) {
+    atomicExch(&p.sched[0], 0);
+    atomicExch(&p.sched[1], 0);
+    __threadfence();
+  }
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Device-side launch helpers live in the per-kernel .cu files.
+template <int D>
+cudaError_t launch_decode(const FwdParams& p, const KvMaps& maps, int grid, cudaStream_t s);
+template <int D>
+cudaError_t launch_prefill(const FwdParams& p, const KvMaps& maps, int grid, cudaStream_t s);
+template <int D>
+cudaError_t launch_combine(const FwdParams& p, cudaStream_t s);
+template <int D>
+cudaError_t launch_gather(const FwdParams& p, const KvMaps& maps, int max_tiles, const int64_t* kv_offsets,
+                          void* k_out, void* v_out, cudaStream_t s);
+template <int D>
+int decode_smem_bytes();
+template <int D>
+int prefill_smem_bytes();
+
+}  // namespace tfa

@@ -1,0 +1,379 @@
+// Decode-shaped paged attention (q_len * group <= 16 packed rows per kv head).
+//
+// One work item = (sequence b, kv head h, kv split). All q heads of the GQA group (and
+// all q tokens of the sequence, for short speculative chunks) are packed into N <= 16
+// columns, so every K/V byte is read from HBM once per kv head. The contractions run on
+// tcgen05 with the kv tile on the M axis:
+//   S^T[128 tok x 16] = K[128 tok x D] . Q^T            (A = K tile, K-major; B = Q, K-major)
+//   O^T[D x 16]      = V^T[D x 128 tok] . P^T           (A = V tile, MN-major; B = P, K-major)
+// Both accumulate in TMEM. Softmax threads own one kv token (TMEM lane) each, reduce the
+// per-column max across the 128 tokens with warp shuffles plus a 4-warp exchange, and
+// write P^T back to shared memory for the second MMA. The un-normalised output of each
+// tile is folded into registers (thread = head-dim lane) with the running rescale.
+//
+// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = MMA issuer + TMEM owner,
+// warps 2-5 = softmax / epilogue.
+#include <cmath>
+
+#include "tfa_common.cuh"
+
+namespace tfa {
+
+namespace {
+
+constexpr int kNP = 16;  // packed q rows (MMA N)
+
+template <int D>
+struct DecodeCfg {
+  static constexpr int kPanels = D / 64;
+  static constexpr int kStages = (D == 128) ? 3 : 6;
+  static constexpr int kStageBytes = KvStage<D>::kBytes;
+  static constexpr int kQBytes = kPanels * kNP * 128;  // Q: kNP rows x D, K-major SW128 panels
+  static constexpr int kPBytes = 2 * kNP * 128;        // P^T: kNP rows x 128 tokens (2 panels)
+  static constexpr int kQOff = kStages * kStageBytes;
+  static constexpr int kPOff = kQOff + kQBytes;          // two P buffers
+  static constexpr int kDynBytes = kPOff + 2 * kPBytes + 1024;  // + alignment slack
+  static constexpr uint32_t kTmemCols = 64;              // S^T x2 (16 cols), O^T x2 (16 cols)
+};
+
+template <int D>
+__global__ void __launch_bounds__(192, 1)
+    decode_kernel(const __grid_constant__ FwdParams p, const __grid_constant__ KvMaps maps) {
+  using Cfg = DecodeCfg<D>;
+  extern __shared__ uint8_t dyn_smem[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dyn_smem) + 1023) & ~uintptr_t(1023));
+  uint8_t* stages = smem;
+  uint8_t* q_smem = smem + Cfg::kQOff;
+  uint8_t* p_smem = smem + Cfg::kPOff;
+
+  __shared__ uint64_t full[Cfg::kStages], empty[Cfg::kStages];
+  __shared__ uint64_t s_full[2], s_free[2], p_full[2], o_full[2], o_free[2];
+  __shared__ uint64_t item_full[2], item_empty[2], q_full[2], red_bar;
+  __shared__ int item_slot[2];
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ volatile int abort_flag;
+  __shared__ float red_max[2][4][kNP];
+  __shared__ float red_sum[2][4][kNP];
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+
+  if (tid == 0) {
+    for (int i = 0; i < Cfg::kStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 4);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&o_full[i], 1);
+      mbar_init(&o_free[i], 4);
+      mbar_init(&item_full[i], 1);
+      mbar_init(&item_empty[i], 5);
+      mbar_init(&q_full[i], 4);
+    }
+    mbar_init(&red_bar, 4);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&maps.k_box);
+    tma_prefetch_desc(&maps.v_box);
+  }
+  if (warp == 1) tmem_alloc(&tmem_base_sh, Cfg::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_sh;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    producer_loop<D, Cfg::kStages>(p, maps, stages, full, empty, item_full, item_empty, item_slot, &abort_flag,
+                                   lane);
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    const uint32_t idesc_qk = make_idesc_bf16_f32(128, kNP, false, false);
+    const uint32_t idesc_pv = make_idesc_bf16_f32(128, kNP, true, false);
+    const uint32_t q_addr = smem_u32(q_smem);
+    int c = 0;
+    bool ok = true;
+    for (int k = 0; ok; ++k) {
+      const int slot = k & 1;
+      if (!mbar_wait(&item_full[slot], (k >> 1) & 1, &abort_flag, p.err, kDevErrTimeoutMma)) break;
+      const int idx = item_slot[slot];
+      if (idx >= p.num_items) break;
+      const Work w = get_work(p, idx);
+      const int n = w.tile_end - w.tile_begin;
+      if (!mbar_wait(&q_full[slot], (k >> 1) & 1, &abort_flag, p.err, kDevErrTimeoutMma)) break;
+      if (lane == 0 && n > 0) {
+        auto issue_qk = [&](int cc) -> bool {
+          const int st = cc % Cfg::kStages;
+          if (!mbar_wait(&full[st], (cc / Cfg::kStages) & 1, &abort_flag, p.err, kDevErrTimeoutMma)) return false;
+          if (!mbar_wait(&s_free[cc & 1], ((cc >> 1) & 1) ^ 1, &abort_flag, p.err, kDevErrTimeoutMma)) return false;
+          tc_fence_after();
+          const uint32_t k_addr = smem_u32(stages + st * Cfg::kStageBytes) + KvStage<D>::kTensorBytes;
+          const uint32_t d_tmem = tmem + (cc & 1) * kNP;
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * KvStage<D>::kPanelBytes + (kk & 3) * 32;
+            const uint32_t qoff = (kk >> 2) * (kNP * 128) + (kk & 3) * 32;
+            umma_bf16_ss(d_tmem, make_sdesc_sw128(k_addr + off, 16, 1024), make_sdesc_sw128(q_addr + qoff, 16, 1024),
+                         idesc_qk, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[cc & 1]);
+          return true;
+        };
+        ok = issue_qk(c);
+        for (int j = 0; ok && j < n; ++j) {
+          const int cj = c + j;
+          if (j + 1 < n && !(ok = issue_qk(cj + 1))) break;
+          if (!mbar_wait(&p_full[cj & 1], (cj >> 1) & 1, &abort_flag, p.err, kDevErrTimeoutMma) ||
+              !mbar_wait(&o_free[cj & 1], ((cj >> 1) & 1) ^ 1, &abort_flag, p.err, kDevErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const int st = cj % Cfg::kStages;
+          const uint32_t v_addr = smem_u32(stages + st * Cfg::kStageBytes);
+          const uint32_t pb = smem_u32(p_smem + (cj & 1) * Cfg::kPBytes);
+          const uint32_t d_tmem = tmem + 32 + (cj & 1) * kNP;
+#pragma unroll
+          for (int kk = 0; kk < kBN / 16; ++kk) {
+            const uint32_t voff = kk * 2048;
+            const uint32_t poff = (kk >> 2) * (kNP * 128) + (kk & 3) * 32;
+            umma_bf16_ss(d_tmem, make_sdesc_sw128(v_addr + voff, KvStage<D>::kPanelBytes, 1024),
+                         make_sdesc_sw128(pb + poff, 16, 1024), idesc_pv, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[st]);
+          umma_commit(&o_full[cj & 1]);
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      c += n;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&item_empty[slot]);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax / epilogue
+    const int sw = warp - 2;                // 0..3 among the softmax warps
+    const int quad = warp & 3;              // TMEM lane quadrant this warp may access
+    const int tl = quad * 32 + lane;        // TMEM lane: kv token within tile / head-dim index
+    const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
+    const int tq = sw * 32 + lane;          // 0..127 softmax thread index
+    int c = 0, bp = 0;
+    // Exchange barrier among the four softmax warps (bounded, unlike bar.sync).
+    auto sm_sync = [&]() -> bool {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&red_bar);
+      const bool r = mbar_wait(&red_bar, bp & 1, &abort_flag, p.err, kDevErrTimeoutSoftmax);
+      ++bp;
+      return r;
+    };
+    for (int k = 0;; ++k) {
+      const int slot = k & 1;
+      if (!mbar_wait(&item_full[slot], (k >> 1) & 1, &abort_flag, p.err, kDevErrTimeoutSoftmax)) break;
+      const int idx = item_slot[slot];
+      if (idx >= p.num_items) break;
+      const Work w = get_work(p, idx);
+      const int n = w.tile_end - w.tile_begin;
+
+      // Q rows -> shared memory (K-major, 128-byte swizzle); rows >= nrows are zero.
+      {
+        const int r = tq >> 3, u = tq & 7;
+#pragma unroll
+        for (int ch = 0; ch < Cfg::kPanels; ++ch) {
+          uint4 val = make_uint4(0, 0, 0, 0);
+          if (r < w.nrows) {
+            const int R = w.row0 + r;
+            const __nv_bfloat16* src = p.q + (int64_t)(w.q0 + R / p.group) * p.q_s0 +
+                                       (int64_t)(w.h * p.group + R % p.group) * p.q_s1 + ch * 64 + u * 8;
+            val = __ldg(reinterpret_cast<const uint4*>(src));
+          }
+          *reinterpret_cast<uint4*>(q_smem + ch * (kNP * 128) + r * 128 + ((u ^ (r & 7)) << 4)) = val;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&q_full[slot]);
+      }
+
+      int lo[kNP], hi[kNP];
+#pragma unroll
+      for (int r = 0; r < kNP; ++r) {
+        if (r < w.nrows) {
+          visible_range(p, (w.row0 + r) / p.group, w.q_len, w.kv_len, lo[r], hi[r]);
+        } else {
+          lo[r] = 1;
+          hi[r] = 0;
+        }
+      }
+      float m[kNP], l[kNP], o[kNP], a_prev[kNP];
+#pragma unroll
+      for (int r = 0; r < kNP; ++r) {
+        m[r] = -INFINITY;
+        l[r] = 0.f;
+        o[r] = 0.f;
+        a_prev[r] = 1.f;
+      }
+      bool ok = true;
+      for (int j = 0; j < n; ++j) {
+        const int cj = c + j;
+        if (!mbar_wait(&s_full[cj & 1], (cj >> 1) & 1, &abort_flag, p.err, kDevErrTimeoutSoftmax)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        float s[kNP];
+        tmem_ld16(lane_base + (cj & 1) * kNP, s);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free[cj & 1]);
+
+        const int pos = (w.tile_begin + j) * kBN + tl;
+        float a[kNP];
+#pragma unroll
+        for (int r = 0; r < kNP; ++r) {
+          s[r] = (pos >= lo[r] && pos <= hi[r]) ? s[r] * p.scale_log2 : -INFINITY;
+          const float wm = warp_max(s[r]);
+          if (lane == 0) red_max[cj & 1][sw][r] = wm;
+        }
+        if (!sm_sync()) {
+          ok = false;
+          break;
+        }
+#pragma unroll
+        for (int r = 0; r < kNP; ++r) {
+          const float tmax = fmaxf(fmaxf(red_max[cj & 1][0][r], red_max[cj & 1][1][r]),
+                                   fmaxf(red_max[cj & 1][2][r], red_max[cj & 1][3][r]));
+          const float mn = fmaxf(m[r], tmax);
+          a[r] = (m[r] == -INFINITY) ? 1.f : ex2_approx(m[r] - mn);
+          const float ms = (mn == -INFINITY) ? 0.f : mn;
+          s[r] = ex2_approx(s[r] - ms);
+          l[r] = l[r] * a[r] + s[r];
+          m[r] = mn;
+        }
+        // fold the previous tile's P.V into the register accumulator
+        if (j > 0) {
+          const int cp = cj - 1;
+          if (!mbar_wait(&o_full[cp & 1], (cp >> 1) & 1, &abort_flag, p.err, kDevErrTimeoutSoftmax)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          float ot[kNP];
+          tmem_ld16(lane_base + 32 + (cp & 1) * kNP, ot);
+          tmem_wait_ld();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&o_free[cp & 1]);
+#pragma unroll
+          for (int r = 0; r < kNP; ++r) o[r] = o[r] * a_prev[r] + ot[r];
+        }
+#pragma unroll
+        for (int r = 0; r < kNP; ++r) a_prev[r] = a[r];
+        // P^T -> shared memory: row r (q row), column tl (kv token), K-major SW128.
+        uint8_t* pb = p_smem + (cj & 1) * Cfg::kPBytes + (tl >> 6) * (kNP * 128);
+        const int cu = (tl & 63) >> 3, ce = (tl & 7) * 2;
+#pragma unroll
+        for (int r = 0; r < kNP; ++r)
+          *reinterpret_cast<__nv_bfloat16*>(pb + r * 128 + ((cu ^ (r & 7)) << 4) + ce) = __float2bfloat16(s[r]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[cj & 1]);
+      }
+      if (ok && n > 0) {
+        const int cl = c + n - 1;
+        if (!mbar_wait(&o_full[cl & 1], (cl >> 1) & 1, &abort_flag, p.err, kDevErrTimeoutSoftmax)) {
+          ok = false;
+        } else {
+          tc_fence_after();
+          float ot[kNP];
+          tmem_ld16(lane_base + 32 + (cl & 1) * kNP, ot);
+          tmem_wait_ld();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&o_free[cl & 1]);
+#pragma unroll
+          for (int r = 0; r < kNP; ++r) o[r] = o[r] * a_prev[r] + ot[r];
+        }
+      }
+      if (!ok) break;
+      c += n;
+
+      // column sums of the per-token partial denominators
+#pragma unroll
+      for (int r = 0; r < kNP; ++r) {
+        const float ws = warp_sum(l[r]);
+        if (lane == 0) red_sum[k & 1][sw][r] = ws;
+      }
+      if (!sm_sync()) break;
+      const bool direct = (w.nsplits == 1);
+#pragma unroll
+      for (int r = 0; r < kNP; ++r) {
+        if (r >= w.nrows) break;
+        const float lsum = red_sum[k & 1][0][r] + red_sum[k & 1][1][r] + red_sum[k & 1][2][r] + red_sum[k & 1][3][r];
+        const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+        const int R = w.row0 + r;
+        const int tok = w.q0 + R / p.group;
+        const int qh = w.h * p.group + R % p.group;
+        const float lse2 = lsum > 0.f ? m[r] + lg2_approx(lsum) : -INFINITY;
+        if (direct) {
+          if (tl < D) p.out[(int64_t)tok * p.o_s0 + (int64_t)qh * p.o_s1 + tl] = __float2bfloat16(o[r] * inv);
+          if (tq == 0 && p.lse) p.lse[(int64_t)tok * p.hq + qh] = lse2 * kLn2;
+        } else {
+          const int64_t row = ((int64_t)w.split * p.total_q + tok) * p.hq + qh;
+          if (tl < D) p.split_o[row * D + tl] = o[r] * inv;
+          if (tq == 0) p.split_lse[row] = lse2;
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&item_empty[slot]);
+    }
+  }
+
+  if (abort_flag && warp == 0) {
+    // Let TMA copies that may still be in flight land before the CTA's shared memory
+    // is released (bounded: 100 us).
+    const uint64_t t0 = global_timer_ns();
+    while (global_timer_ns() - t0 < 100000ull) __nanosleep(1000);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::kTmemCols);
+  }
+  if (tid == 0) scheduler_finish(p);
+}
+
+}  // namespace
+
+template <int D>
+int decode_smem_bytes() {
+  return DecodeCfg<D>::kDynBytes;
+}
+
+template <int D>
+cudaError_t launch_decode(const FwdParams& p, const KvMaps& maps, int grid, cudaStream_t s) {
+  static bool configured[128] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(decode_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         DecodeCfg<D>::kDynBytes);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  decode_kernel<D><<<grid, 192, DecodeCfg<D>::kDynBytes, s>>>(p, maps);
+  return cudaGetLastError();
+}
+
+template int decode_smem_bytes<64>();
+template int decode_smem_bytes<128>();
+template cudaError_t launch_decode<64>(const FwdParams&, const KvMaps&, int, cudaStream_t);
+template cudaError_t launch_decode<128>(const FwdParams&, const KvMaps&, int, cudaStream_t);
+
+}  // namespace tfa

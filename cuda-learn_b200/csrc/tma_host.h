@@ -1,0 +1,53 @@
+// Host-side creation of TMA tensor maps for the paged KV cache.
+//
+// The KV cache of one tensor (K or V) is [num_blocks, block_size, num_kv_heads, head_dim]
+// bf16 with an arbitrary element stride per dimension and a contiguous head_dim. The map
+// is 4-D with the dimensions listed innermost first: (head_dim, kv_head, slot, block).
+// A box is (64 columns, 1 head, rows slots, 1 block) and lands in shared memory as
+// rows x 128 bytes with the 128-byte swizzle, which is the K-major / MN-major SW128
+// operand layout the tcgen05 MMAs read.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdint>
+#include <mutex>
+
+namespace tfa {
+
+inline PFN_cuTensorMapEncodeTiled_v12000 get_encode_tiled() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+  });
+  return fn;
+}
+
+// strides_elems: element strides of (block, slot, kv_head) -- head_dim stride must be 1.
+// Returns 0 on success, a non-zero CUresult (or -1 if the driver entry is missing).
+inline int encode_kv_map(CUtensorMap* map, const void* base, int64_t num_blocks, int64_t block_size,
+                         int64_t num_kv_heads, int64_t head_dim, const int64_t strides_elems[3],
+                         uint32_t box_rows) {
+  auto fn = get_encode_tiled();
+  if (!fn) return -1;
+  cuuint64_t dims[4] = {(cuuint64_t)head_dim, (cuuint64_t)num_kv_heads, (cuuint64_t)block_size,
+                        (cuuint64_t)num_blocks};
+  cuuint64_t strides[3] = {(cuuint64_t)strides_elems[2] * 2, (cuuint64_t)strides_elems[1] * 2,
+                           (cuuint64_t)strides_elems[0] * 2};
+  cuuint32_t box[4] = {64, 1, box_rows, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return (int)r;
+}
+
+}  // namespace tfa

@@ -1,0 +1,242 @@
+"""Parity of the sm_100a forward with the CPU oracle and the reference's golden outputs.
+
+Tolerances (bf16 inputs, fp32 math in the oracle): output max-abs error <= 2e-2,
+natural-log LSE max-abs error <= 1e-3. Calls go through the public
+``flash_attn_varlen_func`` (which calls the C ABI ``tfa_fwd``).
+"""
+
+from __future__ import annotations
+
+import math
+
+import pytest
+import torch
+
+from conftest import golden_files, load_golden
+from oracle.paged_attention import paged_attention_oracle
+from toy_flash_attn import flash_attention_func as faf
+from toy_flash_attn.workloads import PagedCase, baseline_config, reference_case
+
+OUT_TOL = 2e-2
+LSE_TOL = 1e-3
+
+pytestmark = pytest.mark.gpu
+
+
+def run_cuda(case: PagedCase, **kw):
+    c = case.to("cuda")
+    out = torch.empty_like(c.q)
+    lse = torch.empty(c.q.shape[0], c.q.shape[1], dtype=torch.float32, device="cuda")
+    res = faf.flash_attn_varlen_func(**c.kwargs(), out=out, softmax_lse=lse, **kw)
+    assert res.data_ptr() == out.data_ptr()
+    torch.cuda.synchronize()
+    assert faf.read_device_error() == 0
+    return out.cpu(), lse.cpu()
+
+
+def oracle(case: PagedCase):
+    return paged_attention_oracle(case.q, case.k_cache, case.v_cache, case.cu_seqlens_q, case.seqused_k,
+                                  case.block_table, case.causal, case.window_size)
+
+
+def assert_parity(case: PagedCase, **kw):
+    out, lse = run_cuda(case, **kw)
+    ref_out, ref_lse = oracle(case)
+    assert torch.isfinite(out.float()).all(), "non-finite output"
+    err = (out.float() - ref_out).abs().max().item() if out.numel() else 0.0
+    assert err <= OUT_TOL, f"{case.name}: out max-abs err {err}"
+    fin = torch.isfinite(ref_lse)
+    assert torch.equal(fin, torch.isfinite(lse)), f"{case.name}: LSE finiteness differs"
+    if fin.any():
+        lerr = (lse[fin] - ref_lse[fin]).abs().max().item()
+        assert lerr <= LSE_TOL, f"{case.name}: lse max-abs err {lerr}"
+    return out, lse
+
+
+GOLDEN = [p for p in golden_files()]
+
+
+@pytest.mark.parametrize("path", GOLDEN, ids=[p.stem for p in GOLDEN])
+def test_golden_vs_reference_output(path):
+    g = load_golden(path)
+    case = PagedCase(g["name"], g["q"], g["k"], g["v"], g["cu_seqlens_q"], g["seqused_k"], g["block_table"],
+                     g["max_seqlen_q"], g["max_seqlen_k"], g["causal"], g["window_size"])
+    if case.q.shape[2] not in (64, 128):
+        with pytest.raises(RuntimeError, match="TFA_ERR_HEAD_DIM"):
+            run_cuda(case)
+        return
+    out, _ = assert_parity(case)
+    err = (out.float() - g["out_ref_fp32"].float()).abs().max().item()
+    assert err <= OUT_TOL, f"vs reference output: {err}"
+
+
+@pytest.mark.parametrize("name", ["C1", "C2", "C3", "C4"])
+def test_baseline_configs_full_size(name):
+    assert_parity(baseline_config(name))
+
+
+def test_c5_reduced_batch_full_lengths():
+    case = baseline_config("C5", batch=12, num_blocks=40000)
+    assert_parity(case)
+
+
+@pytest.mark.parametrize("splits", [1, 2, 3, 7, 16])
+def test_forced_splits_decode(splits):
+    assert_parity(baseline_config("C2"), num_splits=splits)
+
+
+@pytest.mark.parametrize("splits", [1, 2, 5])
+def test_forced_splits_prefill(splits):
+    assert_parity(baseline_config("C3"), num_splits=splits)
+
+
+@pytest.mark.parametrize("block_size", [1, 2, 4, 8, 16, 32, 64])
+def test_block_sizes(block_size):
+    case = reference_case([1, 3, 40], [300, 77, 129], num_heads=8, num_kv_heads=2, causal=True,
+                          block_size=block_size, seed=block_size)
+    assert_parity(case)
+
+
+@pytest.mark.parametrize("hd", [64, 128])
+@pytest.mark.parametrize("group", [1, 2, 4, 7, 8, 16])
+@pytest.mark.parametrize("q_lens", [[1, 1, 1, 1], [1, 1, 5, 33]], ids=["decode", "mixed"])
+def test_gqa_groups(hd, group, q_lens):
+    hkv = 2
+    case = reference_case(q_lens, [260, 1, 140, 200], num_heads=hkv * group, num_kv_heads=hkv, head_dim=hd,
+                          causal=True, block_size=16, seed=group + hd)
+    assert_parity(case)
+
+
+def test_speculative_decode_rows_packed():
+    # q_len * group <= 16 packs several q tokens into the decode kernel's 16 columns
+    case = reference_case([4, 2, 1], [300, 17, 129], num_heads=8, num_kv_heads=2, causal=True, block_size=16)
+    assert_parity(case)
+
+
+@pytest.mark.parametrize("window", [(0, 0), (1, 0), (16, 0), (127, 0), (128, 0), (300, 0), (5, 3), (64, 64),
+                                    (-1, 10), (10, -1)])
+def test_windows_non_causal_and_causal(window):
+    for causal in (False, True):
+        case = reference_case([1, 7, 150], [500, 90, 150], num_heads=4, num_kv_heads=2, causal=causal,
+                              window_size=window, block_size=16, seed=3)
+        assert_parity(case)
+
+
+def test_empty_and_ragged_sequences():
+    # zero-length kv, zero-length q, kv shorter than q (fully masked causal rows -> 0 / -inf)
+    case = reference_case([3, 0, 4, 1, 6], [0, 5, 2, 1, 130], num_heads=4, num_kv_heads=1, causal=True,
+                          block_size=16, seed=5)
+    case.block_table[case.block_table < 0] = 0  # entries past kv_len are never read
+    out, lse = assert_parity(case)
+    assert torch.all(out[:3] == 0)
+    assert torch.all(torch.isneginf(lse[:3]))
+
+
+def test_nan_slots_are_masked():
+    case = baseline_config("C4", batch=4, kv_range=(17, 300))
+    assert torch.isnan(case.k_cache).any()
+    assert_parity(case)
+
+
+def test_strided_q_and_out_views():
+    case = reference_case([5, 70], [90, 70], num_heads=8, num_kv_heads=2, causal=True, block_size=16, seed=9)
+    c = case.to("cuda")
+    big_q = torch.randn(c.q.shape[0], c.q.shape[1] * 2, c.q.shape[2], device="cuda").to(torch.bfloat16)
+    big_q[:, ::2] = c.q
+    qv = big_q[:, ::2]
+    big_out = torch.zeros(c.q.shape[0], c.q.shape[1], c.q.shape[2] * 2, dtype=torch.bfloat16, device="cuda")
+    ov = big_out[:, :, : c.q.shape[2]]
+    faf.flash_attn_varlen_func(qv, c.k_cache, c.v_cache, c.max_seqlen_q, c.cu_seqlens_q, c.max_seqlen_k, None,
+                               c.seqused_k, c.causal, c.window_size, c.block_table, out=ov)
+    ref, _ = oracle(case)
+    assert (ov.float().cpu() - ref).abs().max().item() <= OUT_TOL
+    assert torch.all(big_out[:, :, c.q.shape[2]:] == 0)
+
+
+def test_repeat_calls_identical():
+    case = baseline_config("C2")
+    a, la = run_cuda(case)
+    b, lb = run_cuda(case)
+    assert torch.equal(a, b) and torch.equal(la, lb)
+
+
+def test_block_permutation_invariance():
+    """Moving pages to new physical ids (and updating the table) changes nothing."""
+    case = baseline_config("C2", num_blocks=512)
+    a, _ = run_cuda(case)
+    perm = torch.randperm(512, generator=torch.Generator().manual_seed(1))
+    moved = PagedCase(case.name, case.q, torch.empty_like(case.k_cache), torch.empty_like(case.v_cache),
+                      case.cu_seqlens_q, case.seqused_k, perm[case.block_table.long()].to(torch.int32),
+                      case.max_seqlen_q, case.max_seqlen_k, case.causal, case.window_size)
+    moved.k_cache[perm] = case.k_cache
+    moved.v_cache[perm] = case.v_cache
+    b, _ = run_cuda(moved)
+    assert torch.equal(a, b)
+
+
+def test_softmax_scale_override():
+    case = reference_case([1, 20], [100, 20], num_heads=4, num_kv_heads=2, causal=True, block_size=16, seed=2)
+    out, lse = run_cuda(case, softmax_scale=0.3)
+    ref, ref_lse = paged_attention_oracle(case.q, case.k_cache, case.v_cache, case.cu_seqlens_q, case.seqused_k,
+                                          case.block_table, True, None, softmax_scale=0.3)
+    assert (out.float() - ref).abs().max().item() <= OUT_TOL
+    assert (lse - ref_lse).abs().max().item() <= LSE_TOL
+
+
+def test_non_paged_varlen_path():
+    """block_table=None: dense varlen K/V (flash_attention_func.py:411-457)."""
+    g = torch.Generator().manual_seed(4)
+    lens_q, lens_k = [3, 64], [40, 64]
+    q = torch.randn(sum(lens_q), 4, 64, generator=g).to(torch.bfloat16)
+    k = torch.randn(sum(lens_k), 2, 64, generator=g).to(torch.bfloat16)
+    v = torch.randn(sum(lens_k), 2, 64, generator=g).to(torch.bfloat16)
+    cq = torch.tensor([0, 3, 67], dtype=torch.int32)
+    ck = torch.tensor([0, 40, 104], dtype=torch.int32)
+    out = faf.flash_attn_varlen_func(q.cuda(), k.cuda(), v.cuda(), 64, cq.cuda(), 64, ck.cuda(), causal=True)
+    # oracle on an equivalent paged layout (one token per block)
+    bt = torch.stack([torch.arange(64) + 0, torch.arange(64) + 40]).to(torch.int32)
+    bt[0, 40:] = 0
+    ref, _ = paged_attention_oracle(q, k.unsqueeze(1), v.unsqueeze(1), cq, torch.tensor(lens_k, dtype=torch.int32),
+                                    bt, True, None)
+    assert (out.float().cpu() - ref).abs().max().item() <= OUT_TOL
+
+
+def test_input_validation_errors():
+    case = reference_case([2], [10], num_heads=4, num_kv_heads=2, block_size=16).to("cuda")
+    with pytest.raises(TypeError):
+        faf.flash_attn_varlen_func(case.q.float(), case.k_cache, case.v_cache, 2, case.cu_seqlens_q, 10, None,
+                                   case.seqused_k, False, None, case.block_table)
+    with pytest.raises(TypeError):
+        faf.flash_attn_varlen_func(case.q, case.k_cache, case.v_cache, 2, case.cu_seqlens_q.long(), 10, None,
+                                   case.seqused_k, False, None, case.block_table)
+    with pytest.raises(ValueError):
+        faf.flash_attn_varlen_func(case.q[:, :3], case.k_cache, case.v_cache, 2, case.cu_seqlens_q, 10, None,
+                                   case.seqused_k, False, None, case.block_table)
+    with pytest.raises(RuntimeError, match="TFA_ERR_HEAD_DIM"):
+        q = torch.zeros(2, 4, 96, dtype=torch.bfloat16, device="cuda")
+        kc = torch.zeros(4, 16, 2, 96, dtype=torch.bfloat16, device="cuda")
+        faf.flash_attn_varlen_func(q, kc, kc, 2, case.cu_seqlens_q, 10, None, case.seqused_k, False, None,
+                                   case.block_table)
+
+
+def test_bad_block_id_reported_not_faulting():
+    case = reference_case([1], [40], num_heads=2, num_kv_heads=1, block_size=16)
+    case.block_table[0, 1] = 10_000  # outside the pool
+    c = case.to("cuda")
+    faf.flash_attn_varlen_func(**c.kwargs())
+    torch.cuda.synchronize()
+    assert faf.read_device_error() == 110
+    assert faf.read_device_error() == 0  # cleared
+
+
+def test_plan_decode_vs_prefill_selection():
+    c2 = baseline_config("C2").to("cuda")
+    p = faf.plan(c2.q, c2.k_cache, c2.v_cache, c2.cu_seqlens_q, c2.seqused_k, c2.block_table, c2.max_seqlen_q,
+                 c2.max_seqlen_k, True)
+    assert p["kernel"] == 0 and p["max_splits"] > 1 and p["combine"] == 1
+    c3 = baseline_config("C3").to("cuda")
+    p = faf.plan(c3.q, c3.k_cache, c3.v_cache, c3.cu_seqlens_q, c3.seqused_k, c3.block_table, c3.max_seqlen_q,
+                 c3.max_seqlen_k, True)
+    assert p["kernel"] == 1 and p["rows_per_tile"] == 128
+    assert p["grid"] <= torch.cuda.get_device_properties(0).multi_processor_count
+    assert math.isfinite(p["workspace_bytes"])

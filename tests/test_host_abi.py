@@ -1,0 +1,156 @@
+"""Host-side checks that need no GPU: the C ABI library loads, exports every symbol
+declared in include/tfa.h, and rejects invalid arguments with the documented codes
+before touching the device. Also the Python-level argument checks."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+from toy_flash_attn import _lib
+from toy_flash_attn import flash_attention_func as faf
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "tfa.h"
+
+
+def declared_symbols() -> set[str]:
+    text = HEADER.read_text()
+    return set(re.findall(r"TFA_API\s+[\w\s\*]+?\b(tfa_\w+)\s*\(", text))
+
+
+def test_header_declares_expected_symbols():
+    assert declared_symbols() == set(_lib.EXPORTED_SYMBOLS)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+
+
+def test_library_exports_nothing_else():
+    import subprocess
+
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.lib_path())], capture_output=True, text=True).stdout
+    funcs = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    assert funcs == declared_symbols()
+
+
+def test_status_strings():
+    lib = _lib.load()
+    for code in _lib.STATUS_NAMES:
+        assert lib.tfa_status_string(code).decode()
+    assert lib.tfa_status_string(12345) == b"unknown status"
+
+
+def _params(**over):
+    p = _lib.TfaFwdParams()
+    buf = ctypes.create_string_buffer(1 << 16)
+    base = (ctypes.addressof(buf) + 255) // 256 * 256
+    p.q = p.k = p.v = p.out = base
+    p.cu_seqlens_q = p.seqused_k = p.block_table = base
+    p.q_stride[:] = [256, 64, 1]
+    p.out_stride[:] = [256, 64, 1]
+    p.k_stride[:] = [16 * 2 * 64, 2 * 64, 64, 1]
+    p.v_stride[:] = [16 * 2 * 64, 2 * 64, 64, 1]
+    p.block_table_stride0 = 8
+    p.batch, p.total_q, p.num_q_heads, p.num_kv_heads = 1, 1, 4, 2
+    p.head_dim, p.block_size, p.num_blocks = 64, 16, 8
+    p.max_seqlen_q, p.max_seqlen_k = 1, 16
+    p.window_left = p.window_right = -1
+    for k, v in over.items():
+        setattr(p, k, v)
+    return p, buf
+
+
+@pytest.mark.parametrize(
+    "over, code",
+    [
+        (dict(head_dim=96), -2),
+        (dict(head_dim=32), -2),
+        (dict(num_q_heads=5), -3),
+        (dict(block_size=24), -4),
+        (dict(block_size=3), -4),
+        (dict(window_left=-2), -6),
+        (dict(num_blocks=0), -6),
+        (dict(q=None), -1),
+        (dict(block_table=None), -1),
+    ],
+)
+def test_fwd_rejects_invalid_arguments(over, code):
+    p, _buf = _params(**over)
+    assert _lib.load().tfa_fwd(ctypes.byref(p), None, 0, None) == code
+
+
+def test_fwd_rejects_misaligned_pointer_and_strides():
+    p, _buf = _params()
+    p.q = p.q + 2
+    assert _lib.load().tfa_fwd(ctypes.byref(p), None, 0, None) == -5
+    p, _buf = _params()
+    p.k_stride[3] = 2
+    assert _lib.load().tfa_fwd(ctypes.byref(p), None, 0, None) == -5
+    p, _buf = _params()
+    p.k_stride[1] = 36  # 72 bytes: not a multiple of 16
+    assert _lib.load().tfa_fwd(ctypes.byref(p), None, 0, None) == -5
+
+
+def test_empty_batch_is_a_no_op():
+    p, _buf = _params(batch=0)
+    assert _lib.load().tfa_fwd(ctypes.byref(p), None, 0, None) == 0
+    p, _buf = _params(total_q=0)
+    assert _lib.load().tfa_fwd(ctypes.byref(p), None, 0, None) == 0
+
+
+def test_plan_without_gpu_uses_b200_sm_count():
+    p, _buf = _params(max_seqlen_k=2048, num_q_heads=14, num_kv_heads=2)
+    info = _lib.TfaPlanInfo()
+    assert _lib.load().tfa_plan(ctypes.byref(p), -1, ctypes.byref(info)) == 0
+    assert info.kernel == 0 and info.rows_per_tile == 16
+    assert info.max_splits == 16 and info.split_cap == 1 and info.combine == 1
+    assert info.grid == min(info.num_items, 148)
+    p.max_seqlen_q = 128
+    assert _lib.load().tfa_plan(ctypes.byref(p), -1, ctypes.byref(info)) == 0
+    assert info.kernel == 1 and info.rows_per_tile == 128 and info.q_tiles == 7
+
+
+def test_workspace_size_grows_with_splits():
+    p, _buf = _params(max_seqlen_k=32768, batch=4, total_q=4)
+    lib = _lib.load()
+    p.num_splits = 1
+    one = lib.tfa_workspace_size(ctypes.byref(p), -1)
+    p.num_splits = 8
+    eight = lib.tfa_workspace_size(ctypes.byref(p), -1)
+    assert one == 256 and eight > one
+    assert eight == 256 + ((8 * 4 * 4 * 4 + 255) // 256) * 256 + 8 * 4 * 4 * 64 * 4
+
+
+def test_python_wrapper_rejects_cpu_tensors():
+    q = torch.zeros(1, 4, 64, dtype=torch.bfloat16)
+    kc = torch.zeros(2, 16, 2, 64, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="expects CUDA tensors"):
+        faf.flash_attn_varlen_func(q, kc, kc, 1, torch.tensor([0, 1], dtype=torch.int32), 16, None,
+                                   torch.tensor([16], dtype=torch.int32), True, None,
+                                   torch.zeros(1, 1, dtype=torch.int32))
+
+
+def test_unsupported_modes_raise(monkeypatch):
+    monkeypatch.setenv("TOY_FLASH_ATTN_USE", "fp32")
+    with pytest.raises(NotImplementedError):
+        faf.flash_attn_varlen_func(None, None, None, 1, None, 1, None, None, False, None, block_table=object())
+
+
+def test_reference_mode_matches_oracle_on_cpu(monkeypatch):
+    """TOY_FLASH_ATTN_USE=reference is the explicitly selected PyTorch path."""
+    from oracle.paged_attention import paged_attention_oracle
+    from toy_flash_attn.workloads import reference_case
+
+    monkeypatch.setenv("TOY_FLASH_ATTN_USE", "reference")
+    case = reference_case([2, 6], [8, 8], causal=True, window_size=(2, 0), dtype=torch.float32)
+    out = faf.flash_attn_varlen_func(**case.kwargs())
+    ref, _ = paged_attention_oracle(case.q, case.k_cache, case.v_cache, case.cu_seqlens_q, case.seqused_k,
+                                    case.block_table, True, (2, 0))
+    torch.testing.assert_close(out, ref, atol=1e-5, rtol=1e-5)
