@@ -298,6 +298,9 @@ def flash_attn_varlen_with_block_cu_bf16(
             _lib.check(lib.tfa_fwd(ctypes.byref(p), ws.data_ptr(), ws.numel(), stream), "tfa_fwd")
         else:
             ev0, ev1 = main_events
+            for ev in (ev0, ev1):
+                if not ev.cuda_event:  # torch creates the event on its first record
+                    ev.record()
             _lib.check(lib.tfa_fwd_timed(ctypes.byref(p), ws.data_ptr(), ws.numel(), stream, ev0.cuda_event,
                                          ev1.cuda_event), "tfa_fwd_timed")
     _maybe_dump_flash_attn_context(
