@@ -158,13 +158,19 @@ def allreduce_max(x: float, world: int) -> float:
 # workloads
 # --------------------------------------------------------------------------------------
 def c5_shard(world: int, rank: int, args):
-    from toy_flash_attn.workloads import baseline_config
+    """This rank's part of C5: a group of kv heads (with their q heads) of every sequence,
+    in the rank's own pool. Only the shard is generated on the device."""
+    from toy_flash_attn.sharding import plan_shards
+    from toy_flash_attn.workloads import baseline_config, c5_kv_lengths
 
     if 8 % world:
         raise SystemExit("C5 shards its 8 kv heads: --gpus must divide 8")
-    hkv = 8 // world
-    return baseline_config("C5", device="cuda", batch=args.batch, num_blocks=args.num_blocks, kv_heads=hkv,
-                           q_heads=4 * hkv)
+    lens = c5_kv_lengths(args.batch or 256)
+    shard = plan_shards(lens, 32, 8, world)[rank]
+    assert shard.sequences == tuple(range(len(lens)))  # heads only: every rank keeps the whole batch
+    hkv = shard.kv_heads[1] - shard.kv_heads[0]
+    return baseline_config("C5", device="cuda", seed=5, batch=args.batch, num_blocks=args.num_blocks,
+                           kv_heads=hkv, q_heads=shard.q_heads[1] - shard.q_heads[0])
 
 
 def call(case, out, lse=None, events=None, num_splits=0):
