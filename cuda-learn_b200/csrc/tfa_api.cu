@@ -7,6 +7,7 @@
 #include "../../include/tfa.h"
 #include "tfa_common.cuh"
 #include "tma_host.h"
+#include "tfa_internal.h"
 
 namespace tfa {
 namespace {
@@ -208,6 +209,8 @@ const char* tfa_status_string(int s) {
     case TFA_ERR_CUDA: return "CUDA call or launch failed";
     case TFA_ERR_DEVICE: return "current device is not an sm_100 GPU";
     case TFA_ERR_KERNEL: return "a kernel reported an error";
+    case TFA_ERR_STATIC_WORKSPACE_LIMIT:
+      return "call needs more workspace than the 32 MiB static workspace of tfa_fwd_static_workspace";
     default: return "unknown status";
   }
 }
@@ -238,7 +241,10 @@ size_t tfa_workspace_size(const tfa_fwd_params* p, int device) {
   return pl.ws_bytes;
 }
 
-namespace {
+}  // extern "C"
+
+namespace tfa {
+// Shared by every forward entry point: checks, plan, descriptors, launches.
 int fwd_impl(const tfa_fwd_params* a, void* workspace, size_t workspace_bytes, void* stream, void* ev_begin,
              void* ev_end) {
   int rc = validate(a);
@@ -269,7 +275,9 @@ int fwd_impl(const tfa_fwd_params* a, void* workspace, size_t workspace_bytes, v
   }
   return TFA_OK;
 }
-}  // namespace
+}  // namespace tfa
+
+extern "C" {
 
 int tfa_fwd(const tfa_fwd_params* a, void* workspace, size_t workspace_bytes, void* stream) {
   return fwd_impl(a, workspace, workspace_bytes, stream, nullptr, nullptr);

@@ -26,6 +26,7 @@ STATUS_NAMES = {
     -9: "TFA_ERR_CUDA",
     -10: "TFA_ERR_DEVICE",
     -11: "TFA_ERR_KERNEL",
+    -12: "TFA_ERR_STATIC_WORKSPACE_LIMIT",
 }
 
 # Every symbol declared in include/tfa.h.
@@ -34,6 +35,7 @@ EXPORTED_SYMBOLS = (
     "tfa_workspace_size",
     "tfa_fwd",
     "tfa_fwd_timed",
+    "tfa_fwd_static_workspace",
     "tfa_read_device_error",
     "tfa_device_sm_count",
     "tfa_status_string",
@@ -127,6 +129,8 @@ def load() -> ctypes.CDLL:
         lib.tfa_fwd.restype = ctypes.c_int
         lib.tfa_fwd_timed.argtypes = [P(TfaFwdParams), _vp, ctypes.c_size_t, _vp, _vp, _vp]
         lib.tfa_fwd_timed.restype = ctypes.c_int
+        lib.tfa_fwd_static_workspace.argtypes = [P(TfaFwdParams), _vp]
+        lib.tfa_fwd_static_workspace.restype = ctypes.c_int
         lib.tfa_read_device_error.argtypes = [_vp, _vp, P(ctypes.c_int)]
         lib.tfa_read_device_error.restype = ctypes.c_int
         lib.tfa_device_sm_count.argtypes = [ctypes.c_int]

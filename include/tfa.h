@@ -49,8 +49,12 @@ typedef enum tfa_status {
   TFA_ERR_TENSOR_MAP = -8,   /* the TMA descriptor for the KV cache could not be encoded */
   TFA_ERR_CUDA = -9,         /* a CUDA runtime call or launch failed */
   TFA_ERR_DEVICE = -10,      /* the current device is not an sm_100 GPU */
-  TFA_ERR_KERNEL = -11       /* a kernel reported an error (see tfa_read_device_error) */
+  TFA_ERR_KERNEL = -11,      /* a kernel reported an error (see tfa_read_device_error) */
+  TFA_ERR_STATIC_WORKSPACE_LIMIT = -12 /* the call needs more workspace than TFA_STATIC_WORKSPACE_BYTES */
 } tfa_status;
+
+/* Size of the fixed device-resident workspace of tfa_fwd_static_workspace (32 MiB). */
+#define TFA_STATIC_WORKSPACE_BYTES (32u * 1024u * 1024u)
 
 /* Arguments of one forward call. Strides are in elements. */
 typedef struct tfa_fwd_params {
@@ -118,6 +122,22 @@ TFA_API int tfa_fwd(const tfa_fwd_params* p, void* workspace, size_t workspace_b
  * when there is one, runs after main_end). Profiling aid; no counterpart in the reference. */
 TFA_API int tfa_fwd_timed(const tfa_fwd_params* p, void* workspace, size_t workspace_bytes, void* stream,
                           void* main_begin, void* main_end);
+
+/* The forward for callers that cannot allocate device memory: a serving loop that must
+ * not call cudaMalloc once it is running (cudaMalloc can synchronise the device and can
+ * fail when memory is fragmented), or a host in another language that binds this C ABI
+ * but has no device allocator to create the workspace tfa_fwd needs. Same arguments,
+ * checks and results as tfa_fwd, but the split-KV workspace is a TFA_STATIC_WORKSPACE_BYTES
+ * array in the library's own device memory (present on every GPU where the library is
+ * loaded, until exit); nothing is allocated. Calls needing a larger workspace
+ * (tfa_workspace_size) return TFA_ERR_STATIC_WORKSPACE_LIMIT. All calls on a device share
+ * the array, so calls that can overlap on the GPU race and must not be issued. The first
+ * call on a device looks up the array's address with that device current and should come
+ * before any stream capture. Error words are read with tfa_read_device_error only for
+ * caller-owned workspaces, so this entry's kernel errors are not reported.
+ * No counterpart in the reference (its op allocates its split buffers on every call,
+ * v8/flash_attn_func.cu:850-862). */
+TFA_API int tfa_fwd_static_workspace(const tfa_fwd_params* p, void* stream);
 
 /* Synchronises `stream`, copies the device error word of `workspace` into *err (0 = none)
  * and clears it. A non-zero word means a kernel hit an internal time limit or found a

@@ -1,0 +1,83 @@
+"""The allocation-free entry point ``tfa_fwd_static_workspace``.
+
+It exists for callers that cannot allocate device memory (a serving loop that must not
+call cudaMalloc once running, or a foreign-language host that binds the C ABI without a
+device allocator): it uses a fixed array in the library's device memory as its split-KV
+workspace. This file runs last so a failure here never hides the other tests; it also
+passes when run alone in a fresh process.
+
+Check: two calls in a row through the C ABI must agree with the caller-workspace entry
+point ``tfa_fwd`` within the parity tolerance (2e-2 on the output, 1e-3 on the LSE).
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import pytest
+import torch
+
+from toy_flash_attn import _lib
+from toy_flash_attn import flash_attention_func as faf
+from toy_flash_attn.workloads import baseline_config, reference_case
+
+pytestmark = pytest.mark.gpu
+
+OUT_TOL = 2e-2
+LSE_TOL = 1e-3
+STATIC_WS_BYTES = 32 * 1024 * 1024
+
+
+def _params(c, out, lse, num_splits=0):
+    return faf._fill_params(c.q, c.k_cache, c.v_cache, out, c.cu_seqlens_q, c.seqused_k, c.block_table,
+                            c.max_seqlen_q, c.max_seqlen_k, c.causal, c.window_size, lse, None, num_splits)
+
+
+def _static_call(c, num_splits=0):
+    out = torch.full_like(c.q, float("nan"))
+    lse = torch.full((c.q.shape[0], c.q.shape[1]), float("nan"), dtype=torch.float32, device=c.q.device)
+    p = _params(c, out, lse, num_splits)
+    stream = torch.cuda.current_stream().cuda_stream
+    rc = _lib.load().tfa_fwd_static_workspace(ctypes.byref(p), stream)
+    _lib.check(rc, "tfa_fwd_static_workspace")
+    torch.cuda.synchronize()
+    return out, lse
+
+
+@pytest.mark.parametrize(
+    "make, splits",
+    [
+        (lambda: baseline_config("C2"), 0),                 # decode kernel, 16 splits + combine
+        (lambda: baseline_config("C3"), 3),                 # prefill kernel, forced splits + combine
+        (lambda: baseline_config("C4", batch=8), 0),        # sliding window, NaN cache slots
+        (lambda: reference_case([1, 9], [700, 90], num_heads=8, num_kv_heads=2, head_dim=128, causal=True,
+                                block_size=16, seed=3), 0),
+    ],
+    ids=["C2", "C3_split3", "C4_b8", "hd128_mixed"],
+)
+def test_static_workspace_matches_tfa_fwd_twice(make, splits):
+    c = make().to("cuda")
+    ref_out = torch.empty_like(c.q)
+    ref_lse = torch.empty(c.q.shape[0], c.q.shape[1], dtype=torch.float32, device="cuda")
+    faf.flash_attn_varlen_func(**c.kwargs(), out=ref_out, softmax_lse=ref_lse, num_splits=splits)
+    torch.cuda.synchronize()
+    for _ in range(2):  # the array keeps the previous call's contents; results must not depend on it
+        out, lse = _static_call(c, splits)
+        assert torch.isfinite(out.float()).all()
+        assert (out.float() - ref_out.float()).abs().max().item() <= OUT_TOL
+        fin = torch.isfinite(ref_lse)
+        assert torch.equal(fin, torch.isfinite(lse))
+        assert (lse[fin] - ref_lse[fin]).abs().max().item() <= LSE_TOL
+
+
+def test_static_workspace_rejects_oversized_call():
+    # 2048 sequences x 32 q heads x 16 splits x 128 dims of fp32 partials >> 32 MiB
+    c = reference_case([1] * 64, [4096] * 64, num_heads=32, num_kv_heads=8, head_dim=128, causal=True,
+                       block_size=16).to("cuda")
+    out = torch.empty_like(c.q)
+    p = _params(c, out, None, num_splits=32)
+    dev = torch.cuda.current_device()
+    need = _lib.load().tfa_workspace_size(ctypes.byref(p), dev)
+    assert need > STATIC_WS_BYTES
+    rc = _lib.load().tfa_fwd_static_workspace(ctypes.byref(p), torch.cuda.current_stream().cuda_stream)
+    assert _lib.STATUS_NAMES[rc] == "TFA_ERR_STATIC_WORKSPACE_LIMIT"
