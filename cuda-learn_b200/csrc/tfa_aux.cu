@@ -15,6 +15,7 @@ namespace {
 template <int D>
 __global__ void __launch_bounds__(128) combine_kernel(const __grid_constant__ FwdParams p) {
   constexpr int EPL = D / 32;  // elements per lane
+  grid_dependency_wait();      // partials of the attention kernel are complete and visible
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t pair = (int64_t)blockIdx.x * 4 + warp;
   if (pair >= (int64_t)p.total_q * p.hq) return;
@@ -117,8 +118,17 @@ template <int D>
 cudaError_t launch_combine(const FwdParams& p, cudaStream_t s) {
   const int64_t pairs = (int64_t)p.total_q * p.hq;
   const int64_t blocks = (pairs + 3) / 4;
-  combine_kernel<D><<<(unsigned)blocks, 128, 0, s>>>(p);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)blocks);
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, combine_kernel<D>, p);
 }
 
 template <int D>

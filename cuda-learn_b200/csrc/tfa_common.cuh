@@ -135,82 +135,130 @@ struct KvMaps {
   CUtensorMap k_box, k_row, v_box, v_row;
 };
 
-template <int D>
-__device__ __forceinline__ void produce_tile(const FwdParams& p, const KvMaps& maps, const Work& w, int tile,
-                                             uint8_t* stage, uint64_t* full_bar, int lane, uint64_t policy) {
-  if (lane == 0) mbar_arrive_expect_tx(full_bar, KvStage<D>::kBytes);
-  __syncwarp();
+// Page and row count of 16-slot group g (box_rows slots when block_size < 16) of a tile.
+// The block-table load is only issued here; its value is first used in issue_group, so
+// callers can overlap its latency with a pipeline wait.
+struct GroupSrc {
+  int page;   // physical block (or out of range -> zero fill)
+  int slot;   // first slot inside the block
+  int valid;  // rows < kv_len in this group
+};
+
+__device__ __forceinline__ GroupSrc resolve_group(const FwdParams& p, const Work& w, int tile, int g) {
   const int R = p.box_rows;
-  const int groups = kBN / R;
-  const int bs = p.block_size;
-  const int* bt_row = p.block_table + (int64_t)w.b * p.bt_s0;
-  for (int g = lane; g < groups; g += 32) {
-    const int pos = tile * kBN + g * R;
-    int valid = w.kv_len - pos;
-    valid = valid < 0 ? 0 : (valid > R ? R : valid);
-    int page = p.num_blocks;  // out of range -> zero fill
-    const int slot = pos % bs;
-    if (valid > 0) {
-      page = __ldg(bt_row + pos / bs);
-      if (page < 0 || page >= p.num_blocks) {
-        atomicCAS(p.err, 0, (int)kDevErrBadBlockId);
-        page = p.num_blocks;
-        valid = R;  // whole box out of range -> zeros
-      }
-    }
-    const uint32_t v_dst = smem_u32(stage) + g * R * 128;
-    const uint32_t k_dst = v_dst + KvStage<D>::kTensorBytes;
+  const int pos = tile * kBN + g * R;
+  GroupSrc s;
+  int valid = w.kv_len - pos;
+  s.valid = valid < 0 ? 0 : (valid > R ? R : valid);
+  s.slot = pos % p.block_size;
+  s.page = p.num_blocks;
+  if (s.valid > 0) s.page = __ldg(p.block_table + (int64_t)w.b * p.bt_s0 + pos / p.block_size);
+  return s;
+}
+
+template <int D>
+__device__ __forceinline__ void issue_group(const FwdParams& p, const KvMaps& maps, const Work& w, int g, GroupSrc src,
+                                            uint8_t* stage, uint64_t* full_bar, uint64_t policy) {
+  const int R = p.box_rows;
+  int valid = src.valid, page = src.page;
+  if (valid > 0 && (page < 0 || page >= p.num_blocks)) {
+    atomicCAS(p.err, 0, (int)kDevErrBadBlockId);
+    page = p.num_blocks;
+    valid = R;  // whole box out of range -> zeros
+  }
+  const uint32_t v_dst = smem_u32(stage) + g * R * 128;
+  const uint32_t k_dst = v_dst + KvStage<D>::kTensorBytes;
 #pragma unroll
-    for (int ch = 0; ch < KvStage<D>::kPanels; ++ch) {
-      const uint32_t off = ch * KvStage<D>::kPanelBytes;
-      if (valid == R) {
-        tma_load_4d(k_dst + off, &maps.k_box, ch * 64, w.h, slot, page, full_bar, policy);
-        tma_load_4d(v_dst + off, &maps.v_box, ch * 64, w.h, slot, page, full_bar, policy);
-      } else if (valid == 0) {
-        tma_load_4d(k_dst + off, &maps.k_box, ch * 64, w.h, 0, p.num_blocks, full_bar, policy);
-        tma_load_4d(v_dst + off, &maps.v_box, ch * 64, w.h, 0, p.num_blocks, full_bar, policy);
-      } else {
-        for (int r = 0; r < R; ++r) {
-          const int s = r < valid ? slot + r : bs;  // slot index bs is out of range -> zeros
-          tma_load_4d(k_dst + off + r * 128, &maps.k_row, ch * 64, w.h, s, page, full_bar, policy);
-          tma_load_4d(v_dst + off + r * 128, &maps.v_row, ch * 64, w.h, s, page, full_bar, policy);
-        }
+  for (int ch = 0; ch < KvStage<D>::kPanels; ++ch) {
+    const uint32_t off = ch * KvStage<D>::kPanelBytes;
+    if (valid == R) {
+      tma_load_4d(k_dst + off, &maps.k_box, ch * 64, w.h, src.slot, page, full_bar, policy);
+      tma_load_4d(v_dst + off, &maps.v_box, ch * 64, w.h, src.slot, page, full_bar, policy);
+    } else if (valid == 0) {
+      tma_load_4d(k_dst + off, &maps.k_box, ch * 64, w.h, 0, p.num_blocks, full_bar, policy);
+      tma_load_4d(v_dst + off, &maps.v_box, ch * 64, w.h, 0, p.num_blocks, full_bar, policy);
+    } else {
+      for (int r = 0; r < R; ++r) {
+        const int sl = r < valid ? src.slot + r : p.block_size;  // slot index block_size is out of range -> zeros
+        tma_load_4d(k_dst + off + r * 128, &maps.k_row, ch * 64, w.h, sl, page, full_bar, policy);
+        tma_load_4d(v_dst + off + r * 128, &maps.v_row, ch * 64, w.h, sl, page, full_bar, policy);
       }
     }
   }
 }
 
+// Gathers one whole tile (all groups) into `stage`; used where no prefetch is possible.
+template <int D>
+__device__ __forceinline__ void produce_tile(const FwdParams& p, const KvMaps& maps, const Work& w, int tile,
+                                             uint8_t* stage, uint64_t* full_bar, int lane, uint64_t policy) {
+  if (lane == 0) mbar_arrive_expect_tx(full_bar, KvStage<D>::kBytes);
+  __syncwarp();
+  const int groups = kBN / p.box_rows;
+  for (int g = lane; g < groups; g += 32)
+    issue_group<D>(p, maps, w, g, resolve_group(p, w, tile, g), stage, full_bar, policy);
+}
+
 // Producer warp main loop shared by both kernels. Fetches work items dynamically,
-// publishes each into the two-slot item queue and streams their kv tiles.
+// publishes each into the two-slot item queue and streams their kv tiles. When a tile
+// has at most 32 groups (block_size >= 4), lane g owns group g and the block-table
+// entries of tile t+1 are requested before the wait for tile t's free stage, so the
+// table latency hides behind the pipeline; the next item is claimed while the last tile
+// of the current one waits for its stage. The first item of CTA i is item i; later items
+// come from the shared counter offset by the grid size, so start-up has no atomic.
 template <int D, int STAGES>
 __device__ __forceinline__ void producer_loop(const FwdParams& p, const KvMaps& maps, uint8_t* stages,
                                               uint64_t* full, uint64_t* empty, uint64_t* item_full,
                                               uint64_t* item_empty, int* item_slot, volatile int* abort_flag,
                                               int lane) {
   const uint64_t policy = l2_policy_evict_first();
+  const int groups = kBN / p.box_rows;
+  const bool lane_per_group = groups <= 32;
   int c = 0;
+  int claimed = (lane == 0) ? (int)blockIdx.x : 0;  // next item index (lane 0)
+  auto claim = [&]() {
+    if (lane == 0) claimed = atomicAdd(&p.sched[0], 1) + (int)gridDim.x;
+  };
   for (int k = 0;; ++k) {
     const int slot = k & 1;
     if (!mbar_wait(&item_empty[slot], ((k >> 1) & 1) ^ 1, abort_flag, p.err, kDevErrTimeoutProducer)) return;
-    int idx = 0;
+    int idx = __shfl_sync(0xffffffffu, claimed, 0);
     Work w;
     // Skip split slots a sequence does not use without bothering the consumers.
-    for (;;) {
-      if (lane == 0) idx = atomicAdd(&p.sched[0], 1);
-      idx = __shfl_sync(0xffffffffu, idx, 0);
-      if (idx >= p.num_items) break;
+    while (idx < p.num_items) {
       w = get_work(p, idx);
       if (w.exists) break;
+      claim();
+      idx = __shfl_sync(0xffffffffu, claimed, 0);
     }
     if (lane == 0) {
       item_slot[slot] = idx;
       mbar_arrive(&item_full[slot]);
     }
     if (idx >= p.num_items) return;
-    for (int t = w.tile_begin; t < w.tile_end; ++t, ++c) {
-      const int st = c % STAGES;
-      if (!mbar_wait(&empty[st], ((c / STAGES) & 1) ^ 1, abort_flag, p.err, kDevErrTimeoutProducer)) return;
-      produce_tile<D>(p, maps, w, t, stages + st * KvStage<D>::kBytes, &full[st], lane, policy);
+    if (w.tile_end == w.tile_begin) claim();
+    if (lane_per_group) {
+      GroupSrc cur{}, nxt{};
+      if (lane < groups) cur = resolve_group(p, w, w.tile_begin, lane);
+      for (int t = w.tile_begin; t < w.tile_end; ++t, ++c) {
+        if (t + 1 < w.tile_end) {
+          if (lane < groups) nxt = resolve_group(p, w, t + 1, lane);
+        } else {
+          claim();
+        }
+        const int st = c % STAGES;
+        if (!mbar_wait(&empty[st], ((c / STAGES) & 1) ^ 1, abort_flag, p.err, kDevErrTimeoutProducer)) return;
+        if (lane == 0) mbar_arrive_expect_tx(&full[st], KvStage<D>::kBytes);
+        __syncwarp();
+        if (lane < groups) issue_group<D>(p, maps, w, lane, cur, stages + st * KvStage<D>::kBytes, &full[st], policy);
+        cur = nxt;
+      }
+    } else {
+      for (int t = w.tile_begin; t < w.tile_end; ++t, ++c) {
+        if (t + 1 == w.tile_end) claim();
+        const int st = c % STAGES;
+        if (!mbar_wait(&empty[st], ((c / STAGES) & 1) ^ 1, abort_flag, p.err, kDevErrTimeoutProducer)) return;
+        produce_tile<D>(p, maps, w, t, stages + st * KvStage<D>::kBytes, &full[st], lane, policy);
+      }
     }
   }
 }
@@ -225,6 +273,13 @@ __device__ __forceinline__ void scheduler_finish(const FwdParams& p) {
     __threadfence();
   }
 }
+
+// Programmatic dependent launch: lets the next kernel on the stream (the split-KV combine)
+// be scheduled before this grid finishes; the dependent waits with grid_dependency_wait().
+__device__ __forceinline__ void allow_dependent_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll

@@ -87,6 +87,7 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_base_sh;
+  if (tid == 0) allow_dependent_launch();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
