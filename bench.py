@@ -37,6 +37,9 @@ import torch  # noqa: E402
 METRIC = "decode attn KV-read HBM TB/s (C5 large-batch decode)"
 UNIT = "TB/s"
 L2_BYTES = 126 * 1024 * 1024
+# DRAM bytes (read + write) of one decode_kernel launch per algorithmic K/V byte, from the
+# ncu capture summarised in profiles/decode_kernel_C5.md (reduced C5, scaled by K/V bytes).
+TRAFFIC_PER_KV_BYTE = (471.92e6 + 3.99e6) / 471.49e6
 
 
 def parse_args():
@@ -462,7 +465,8 @@ def run_ours(args):
             "roofline": {
                 "kernel": "decode_kernel (tfa_decode.cu)", "bound": "hbm", "achieved": achieved_gbs,
                 "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved_gbs / pk["hbm_gbs"],
-                "peak_source": pk["source"], "traffic": None,
+                "peak_source": pk["source"], "traffic": kvb_local * TRAFFIC_PER_KV_BYTE,
+                "traffic_unit": "bytes per launch (ncu, scaled from reduced C5)",
                 "note": "achieved = algorithmic K/V bytes per launch / mean CUDA-event duration of the attention "
                         "kernel alone (tfa_fwd_timed), max over ranks",
             },
