@@ -287,7 +287,7 @@ def side_configs(pk: dict) -> dict:
     from toy_flash_attn.workloads import baseline_config, kv_bytes, prefill_flops
 
     res = {}
-    for name in ("C1", "C2", "C3", "C4"):
+    for name in ("C1", "C2", "C3", "C4", "P1", "P2"):
         case = baseline_config(name, device="cuda")
         us = time_graph_cold(case)
         p = plan_of(case)
@@ -299,6 +299,8 @@ def side_configs(pk: dict) -> dict:
         else:
             tf = prefill_flops(case) / (us * 1e-6) / 1e12
             entry.update({"TFLOPs": round(tf, 2), "tensor_frac": round(tf / pk["bf16_tflops"], 4)})
+        if name.startswith("P"):
+            entry["scaled"] = "not a BASELINE configuration: long-prompt prefill to show tensor-pipe use"
         res[name] = entry
         del case
         torch.cuda.empty_cache()

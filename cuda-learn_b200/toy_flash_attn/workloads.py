@@ -125,6 +125,10 @@ BASELINE_CONFIGS = {
     "C3": "qwen_varlen_prefill: b4 L[512,384,256,128] 14q/2kv d64 bs16 causal",
     "C4": "sliding_window_decode: b16 kv U[2048,8192] window(1024,0) 32q/8kv d64 bs16 NaN slots",
     "C5": "large_batch_decode: b256 kv logU[1024,32768] 32q/8kv d128 bs16 pool 2^21 blocks",
+    # scaled prefill points (not BASELINE configurations): long causal prompts that make
+    # the prefill kernel compute-bound, to show tensor-pipe utilisation
+    "P1": "scaled_prefill_d128: b1 L8192 32q/8kv d128 bs16 causal",
+    "P2": "scaled_prefill_d64: b4 L4096 14q/2kv d64 bs16 causal",
 }
 
 
@@ -168,7 +172,7 @@ def baseline_config(
     Lengths and block tables are drawn from a CPU generator (the same on every device);
     q/K/V values from a generator on ``device``."""
     name = name.upper()
-    seed = {"C1": 1, "C2": 2, "C3": 3, "C4": 4, "C5": 5}[name] if seed is None else seed
+    seed = {"C1": 1, "C2": 2, "C3": 3, "C4": 4, "C5": 5, "P1": 11, "P2": 12}[name] if seed is None else seed
     dev = torch.device(device)
     gc = torch.Generator().manual_seed(seed)
     bs = 16
@@ -186,6 +190,16 @@ def baseline_config(
         hq, hkv, d = 14, 2, 64
         q_lens = kv_lens = [512, 384, 256, 128]
         nb = num_blocks or 256
+        causal, window, nan_fill = True, None, False
+    elif name == "P1":
+        hq, hkv, d = 32, 8, 128
+        q_lens = kv_lens = [8192] * (batch or 1)
+        nb = num_blocks or sum(n // bs for n in kv_lens) + 64
+        causal, window, nan_fill = True, None, False
+    elif name == "P2":
+        hq, hkv, d = 14, 2, 64
+        q_lens = kv_lens = [4096] * (batch or 4)
+        nb = num_blocks or sum(n // bs for n in kv_lens) + 64
         causal, window, nan_fill = True, None, False
     elif name == "C4":
         hq, hkv, d = 32, 8, 64

@@ -75,6 +75,12 @@ def test_baseline_configs_full_size(name):
     assert_parity(baseline_config(name))
 
 
+def test_long_prefill_d128_gqa():
+    case = reference_case([1536], [1536], num_heads=8, num_kv_heads=2, head_dim=128, causal=True, block_size=16,
+                          seed=21)
+    assert_parity(case)
+
+
 def test_c5_reduced_batch_full_lengths():
     case = baseline_config("C5", batch=12, num_blocks=40000)
     assert_parity(case)
