@@ -71,9 +71,18 @@ int make_plan(const tfa_fwd_params* p, int device, Plan* pl) {
   const int64_t G = p->num_q_heads / p->num_kv_heads;
   const bool decode = p->max_seqlen_q * G <= 16;
   pl->kernel = decode ? 0 : 1;
-  pl->rows = decode ? 16 : 128;
+  // prefill: two 128-row q tiles per work item, unless that leaves too few items to fill
+  // the GPU, in which case each item carries one 128-row tile
+  pl->rows = decode ? 16 : 256;
   int64_t qt = (p->max_seqlen_q * G + pl->rows - 1) / pl->rows;
   if (qt < 1) qt = 1;
+  if (!decode) {
+    const int sms_now = sm_count(device);
+    if ((int64_t)p->batch * p->num_kv_heads * qt < 2 * (int64_t)sms_now) {
+      pl->rows = 128;
+      qt = (p->max_seqlen_q * G + pl->rows - 1) / pl->rows;
+    }
+  }
   pl->q_tiles = (int)qt;
   // kv span one q tile can attend to
   int64_t span = p->max_seqlen_k;

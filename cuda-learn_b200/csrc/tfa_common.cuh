@@ -156,9 +156,12 @@ __device__ __forceinline__ GroupSrc resolve_group(const FwdParams& p, const Work
   return s;
 }
 
+// Issues the TMA boxes of one group of one tensor (K or V) into `dst` (the group's first
+// row inside a 128-row panel set).
 template <int D>
-__device__ __forceinline__ void issue_group(const FwdParams& p, const KvMaps& maps, const Work& w, int g, GroupSrc src,
-                                            uint8_t* stage, uint64_t* full_bar, uint64_t policy) {
+__device__ __forceinline__ void issue_group_tensor(const FwdParams& p, const CUtensorMap* box, const CUtensorMap* row,
+                                                   const Work& w, GroupSrc src, uint32_t dst, uint64_t* full_bar,
+                                                   uint64_t policy) {
   const int R = p.box_rows;
   int valid = src.valid, page = src.page;
   if (valid > 0 && (page < 0 || page >= p.num_blocks)) {
@@ -166,25 +169,29 @@ __device__ __forceinline__ void issue_group(const FwdParams& p, const KvMaps& ma
     page = p.num_blocks;
     valid = R;  // whole box out of range -> zeros
   }
-  const uint32_t v_dst = smem_u32(stage) + g * R * 128;
-  const uint32_t k_dst = v_dst + KvStage<D>::kTensorBytes;
 #pragma unroll
   for (int ch = 0; ch < KvStage<D>::kPanels; ++ch) {
-    const uint32_t off = ch * KvStage<D>::kPanelBytes;
+    const uint32_t off = dst + ch * KvStage<D>::kPanelBytes;
     if (valid == R) {
-      tma_load_4d(k_dst + off, &maps.k_box, ch * 64, w.h, src.slot, page, full_bar, policy);
-      tma_load_4d(v_dst + off, &maps.v_box, ch * 64, w.h, src.slot, page, full_bar, policy);
+      tma_load_4d(off, box, ch * 64, w.h, src.slot, page, full_bar, policy);
     } else if (valid == 0) {
-      tma_load_4d(k_dst + off, &maps.k_box, ch * 64, w.h, 0, p.num_blocks, full_bar, policy);
-      tma_load_4d(v_dst + off, &maps.v_box, ch * 64, w.h, 0, p.num_blocks, full_bar, policy);
+      tma_load_4d(off, box, ch * 64, w.h, 0, p.num_blocks, full_bar, policy);
     } else {
       for (int r = 0; r < R; ++r) {
         const int sl = r < valid ? src.slot + r : p.block_size;  // slot index block_size is out of range -> zeros
-        tma_load_4d(k_dst + off + r * 128, &maps.k_row, ch * 64, w.h, sl, page, full_bar, policy);
-        tma_load_4d(v_dst + off + r * 128, &maps.v_row, ch * 64, w.h, sl, page, full_bar, policy);
+        tma_load_4d(off + r * 128, row, ch * 64, w.h, sl, page, full_bar, policy);
       }
     }
   }
+}
+
+template <int D>
+__device__ __forceinline__ void issue_group(const FwdParams& p, const KvMaps& maps, const Work& w, int g, GroupSrc src,
+                                            uint8_t* stage, uint64_t* full_bar, uint64_t policy) {
+  const uint32_t v_dst = smem_u32(stage) + g * p.box_rows * 128;
+  const uint32_t k_dst = v_dst + KvStage<D>::kTensorBytes;
+  issue_group_tensor<D>(p, &maps.k_box, &maps.k_row, w, src, k_dst, full_bar, policy);
+  issue_group_tensor<D>(p, &maps.v_box, &maps.v_row, w, src, v_dst, full_bar, policy);
 }
 
 // Gathers one whole tile (all groups) into `stage`; used where no prefetch is possible.
@@ -258,6 +265,60 @@ __device__ __forceinline__ void producer_loop(const FwdParams& p, const KvMaps& 
         const int st = c % STAGES;
         if (!mbar_wait(&empty[st], ((c / STAGES) & 1) ^ 1, abort_flag, p.err, kDevErrTimeoutProducer)) return;
         produce_tile<D>(p, maps, w, t, stages + st * KvStage<D>::kBytes, &full[st], lane, policy);
+      }
+    }
+  }
+}
+
+// Producer variant with separate K and V slots: tile t's K goes to slot (2u) % NSLOTS and
+// its V to slot (2u + 1) % NSLOTS, u counting tiles, each slot KvStage<D>::kTensorBytes.
+// Used by the prefill kernel, which keeps K_t and V_t alive for different lengths of time.
+template <int D, int NSLOTS>
+__device__ __forceinline__ void producer_loop_kv_slots(const FwdParams& p, const KvMaps& maps, uint8_t* slots,
+                                                       uint64_t* full, uint64_t* empty, uint64_t* item_full,
+                                                       uint64_t* item_empty, int* item_slot,
+                                                       volatile int* abort_flag, int lane) {
+  constexpr int kSlotBytes = KvStage<D>::kTensorBytes;
+  const uint64_t policy = l2_policy_evict_first();
+  const int groups = kBN / p.box_rows;
+  int c = 0;  // slot loads issued
+  int claimed = (lane == 0) ? (int)blockIdx.x : 0;
+  auto claim = [&]() {
+    if (lane == 0) claimed = atomicAdd(&p.sched[0], 1) + (int)gridDim.x;
+  };
+  for (int k = 0;; ++k) {
+    const int slot = k & 1;
+    if (!mbar_wait(&item_empty[slot], ((k >> 1) & 1) ^ 1, abort_flag, p.err, kDevErrTimeoutProducer)) return;
+    int idx = __shfl_sync(0xffffffffu, claimed, 0);
+    Work w;
+    while (idx < p.num_items) {
+      w = get_work(p, idx);
+      if (w.exists) break;
+      claim();
+      idx = __shfl_sync(0xffffffffu, claimed, 0);
+    }
+    if (lane == 0) {
+      item_slot[slot] = idx;
+      mbar_arrive(&item_full[slot]);
+    }
+    if (idx >= p.num_items) return;
+    if (w.tile_end == w.tile_begin) claim();
+    for (int t = w.tile_begin; t < w.tile_end; ++t) {
+      if (t + 1 == w.tile_end) claim();
+#pragma unroll 1
+      for (int which = 0; which < 2; ++which, ++c) {
+        const int st = c % NSLOTS;
+        if (!mbar_wait(&empty[st], ((c / NSLOTS) & 1) ^ 1, abort_flag, p.err, kDevErrTimeoutProducer)) return;
+        if (lane == 0) mbar_arrive_expect_tx(&full[st], kSlotBytes);
+        __syncwarp();
+        const uint32_t base = smem_u32(slots + st * kSlotBytes);
+        for (int g = lane; g < groups; g += 32) {
+          const GroupSrc src = resolve_group(p, w, t, g);
+          if (which == 0)
+            issue_group_tensor<D>(p, &maps.k_box, &maps.k_row, w, src, base + g * p.box_rows * 128, &full[st], policy);
+          else
+            issue_group_tensor<D>(p, &maps.v_box, &maps.v_row, w, src, base + g * p.box_rows * 128, &full[st], policy);
+        }
       }
     }
   }

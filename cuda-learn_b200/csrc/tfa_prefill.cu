@@ -1,17 +1,26 @@
 // Prefill-shaped paged attention (any q length; used when q_len * group > 16).
 //
-// One work item = (sequence b, kv head h, q tile of 128 packed rows, kv split). A packed
-// row is one (q token, q head of the GQA group) pair, so the rows of a tile share the
-// kv head and every K/V tile is read once for the whole group. Per kv tile:
-//   S[128 x 128] = Q[128 x D] . K^T        (tcgen05, A = Q K-major, B = K tile K-major)
-//   O[128 x D]  += P[128 x 128] . V        (tcgen05, A = P K-major,  B = V tile MN-major)
-// S is double-buffered in TMEM so the QK^T of tile j+1 overlaps the softmax of tile j.
-// Softmax threads own one row each (TMEM lane = row): the row max and sum need no
-// cross-thread exchange. O stays in TMEM; when a warp's running max moves, that warp
-// rescales its O rows in TMEM before the next P.V is issued.
+// One work item = (sequence b, kv head h, q tile pair of 2 x 128 packed rows, kv split).
+// A packed row is one (q token, q head of the GQA group) pair, so all rows of an item
+// share the kv head and every K/V tile is read once for the whole group. The two 128-row
+// tiles A and B each have their own softmax warpgroup, and the MMA warp interleaves them
+// so that one tile's softmax runs while the tensor core works on the other tile:
 //
-// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = MMA issuer + TMEM owner,
-// warps 2-5 = softmax / epilogue.
+//   tensor core:  PV_A(j) QK_A(j+1) PV_B(j) QK_B(j+1) PV_A(j+1) ...
+//   softmax A:              [softmax A(j+1) ..........]
+//   softmax B:                                [softmax B(j+1) ..........]
+//
+// Per kv tile and q tile:
+//   S[128 x 128] = Q[128 x D] . K^T   (tcgen05, A = Q K-major, B = K K-major), S in TMEM
+//   O[128 x D]  += P[128 x 128] . V   (tcgen05, A = P K-major, B = V MN-major), O in TMEM
+// Softmax threads own one row each (TMEM lane = row): pass 1 reads S for the row max,
+// pass 2 reads it again to form P (bf16, written to swizzled shared memory) and the row
+// sum. O is rescaled in TMEM only when a row's max grows by more than 2^8 over the max
+// its P values are referenced to (values of P stay <= 256, far inside bf16/fp32 range),
+// so most tiles need no O round trip.
+//
+// Warps (320 threads): 0 = TMA producer (K and V in separate slots), 1 = MMA issuer and
+// TMEM owner, 2-5 = softmax/epilogue of tile A, 6-9 = softmax/epilogue of tile B.
 #include <cmath>
 
 #include "tfa_common.cuh"
@@ -20,36 +29,38 @@ namespace tfa {
 
 namespace {
 
-constexpr int kRows = 128;
+constexpr int kRows = 128;                // rows per q tile
+constexpr float kRescaleThreshold = 8.f;  // log2 units
 
 template <int D>
 struct PrefillCfg {
   static constexpr int kPanels = D / 64;
-  static constexpr int kStages = (D == 128) ? 2 : 4;
-  static constexpr int kStageBytes = KvStage<D>::kBytes;
-  static constexpr int kQBytes = kPanels * kRows * 128;  // 16 KB per 64 columns
-  static constexpr int kPBytes = 2 * kRows * 128;        // 128 rows x 128 tokens bf16
-  static constexpr int kQOff = kStages * kStageBytes;
-  static constexpr int kPOff = kQOff + kQBytes;
-  static constexpr int kDynBytes = kPOff + kPBytes + 1024;
-  static constexpr uint32_t kTmemCols = 512;             // S x2 (256 cols) + O (D cols)
-  static constexpr uint32_t kOCol = 256;
+  static constexpr int kSlotBytes = KvStage<D>::kTensorBytes;  // one K or V tile
+  static constexpr int kSlots = (D == 128) ? 3 : 6;
+  static constexpr int kQBytes = kPanels * kRows * 128;        // per q tile
+  static constexpr int kPBytes = 2 * kRows * 128;              // 128 rows x 128 tokens bf16
+  static constexpr int kQOff = kSlots * kSlotBytes;
+  static constexpr int kPOff = kQOff + 2 * kQBytes;
+  static constexpr int kDynBytes = kPOff + 2 * kPBytes + 1024;
+  static constexpr uint32_t kTmemCols = 512;                   // S_A, S_B, O_A, O_B
 };
 
+__device__ __forceinline__ uint32_t s_col_of(int x) { return x == 0 ? 0u : 128u; }
+__device__ __forceinline__ uint32_t o_col_of(int x) { return x == 0 ? 256u : 384u; }
+
 template <int D>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     prefill_kernel(const __grid_constant__ FwdParams p, const __grid_constant__ KvMaps maps) {
   using Cfg = PrefillCfg<D>;
   extern __shared__ uint8_t dyn_smem[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dyn_smem) + 1023) & ~uintptr_t(1023));
-  uint8_t* stages = smem;
+  uint8_t* slots = smem;
   uint8_t* q_smem = smem + Cfg::kQOff;
   uint8_t* p_smem = smem + Cfg::kPOff;
 
-  __shared__ uint64_t full[Cfg::kStages], empty[Cfg::kStages];
-  __shared__ uint64_t s_full[2], s_free[2];
-  __shared__ uint64_t p_full, o_full, o_free, q_full[2];
-  __shared__ uint64_t item_full[2], item_empty[2];
+  __shared__ uint64_t full[Cfg::kSlots], empty[Cfg::kSlots];
+  __shared__ uint64_t s_full[2], p_full[2], o_full[2], o_free[2];
+  __shared__ uint64_t item_full[2], item_empty[2], q_full[2];
   __shared__ int item_slot[2];
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_flag;
@@ -59,20 +70,19 @@ __global__ void __launch_bounds__(192, 1)
   const int lane = tid & 31;
 
   if (tid == 0) {
-    for (int i = 0; i < Cfg::kStages; ++i) {
+    for (int i = 0; i < Cfg::kSlots; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 4);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&o_full[i], 1);
+      mbar_init(&o_free[i], 4);
       mbar_init(&item_full[i], 1);
-      mbar_init(&item_empty[i], 5);
-      mbar_init(&q_full[i], 4);
+      mbar_init(&item_empty[i], 9);
+      mbar_init(&q_full[i], 8);
     }
-    mbar_init(&p_full, 4);
-    mbar_init(&o_full, 1);
-    mbar_init(&o_free, 4);
     abort_flag = 0;
     fence_barrier_init();
   }
@@ -88,16 +98,44 @@ __global__ void __launch_bounds__(192, 1)
   if (tid == 0) allow_dependent_launch();
 
   if (warp == 0) {
-    producer_loop<D, Cfg::kStages>(p, maps, stages, full, empty, item_full, item_empty, item_slot, &abort_flag,
-                                   lane);
+    producer_loop_kv_slots<D, Cfg::kSlots>(p, maps, slots, full, empty, item_full, item_empty, item_slot,
+                                           &abort_flag, lane);
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     const uint32_t idesc_qk = make_idesc_bf16_f32(128, 128, false, false);
     const uint32_t idesc_pv = make_idesc_bf16_f32(128, D, false, true);
     const uint32_t q_addr = smem_u32(q_smem);
     const uint32_t p_addr = smem_u32(p_smem);
-    int c = 0, oi = 0;
+    int c = 0;           // slot loads consumed (2 per kv tile)
+    int ts0 = 0, ts1 = 0;  // kv tiles processed per q tile (phase counters)
+    int oi0 = 0, oi1 = 0;  // non-empty items per q tile
     bool ok = true;
+    auto slot_wait = [&](int cc) -> bool {
+      return mbar_wait(&full[cc % Cfg::kSlots], (cc / Cfg::kSlots) & 1, &abort_flag, p.err, kDevErrTimeoutMma);
+    };
+    auto issue_qk = [&](int x, int kslot) {
+      const uint32_t k_addr = smem_u32(slots + kslot * Cfg::kSlotBytes);
+      const uint32_t qx = q_addr + x * Cfg::kQBytes;
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const uint32_t off = (kk >> 2) * KvStage<D>::kPanelBytes + (kk & 3) * 32;
+        umma_bf16_ss(tmem + s_col_of(x), make_sdesc_sw128(qx + off, 16, 1024),
+                     make_sdesc_sw128(k_addr + off, 16, 1024), idesc_qk, kk > 0 ? 1u : 0u);
+      }
+      umma_commit(&s_full[x]);
+    };
+    auto issue_pv = [&](int x, int vslot, bool first) {
+      const uint32_t v_addr = smem_u32(slots + vslot * Cfg::kSlotBytes);
+      const uint32_t px = p_addr + x * Cfg::kPBytes;
+#pragma unroll
+      for (int kk = 0; kk < kBN / 16; ++kk) {
+        const uint32_t poff = (kk >> 2) * (kRows * 128) + (kk & 3) * 32;
+        umma_bf16_ss(tmem + o_col_of(x), make_sdesc_sw128(px + poff, 16, 1024),
+                     make_sdesc_sw128(v_addr + kk * 2048, KvStage<D>::kPanelBytes, 1024), idesc_pv,
+                     (!first || kk > 0) ? 1u : 0u);
+      }
+      umma_commit(&o_full[x]);
+    };
     for (int k = 0; ok; ++k) {
       const int slot = k & 1;
       if (!mbar_wait(&item_full[slot], (k >> 1) & 1, &abort_flag, p.err, kDevErrTimeoutMma)) break;
@@ -105,62 +143,70 @@ __global__ void __launch_bounds__(192, 1)
       if (idx >= p.num_items) break;
       const Work w = get_work(p, idx);
       const int n = w.tile_end - w.tile_begin;
+      const int nx = w.nrows > kRows ? 2 : 1;  // q tiles with rows
       if (!mbar_wait(&q_full[slot], (k >> 1) & 1, &abort_flag, p.err, kDevErrTimeoutMma)) break;
       if (lane == 0 && n > 0) {
-        auto issue_qk = [&](int cc) -> bool {
-          const int st = cc % Cfg::kStages;
-          if (!mbar_wait(&full[st], (cc / Cfg::kStages) & 1, &abort_flag, p.err, kDevErrTimeoutMma)) return false;
-          if (!mbar_wait(&s_free[cc & 1], ((cc >> 1) & 1) ^ 1, &abort_flag, p.err, kDevErrTimeoutMma)) return false;
+        // QK of the first kv tile for both q tiles
+        ok = slot_wait(c);
+        if (ok) {
           tc_fence_after();
-          const uint32_t k_addr = smem_u32(stages + st * Cfg::kStageBytes) + KvStage<D>::kTensorBytes;
-          const uint32_t d_tmem = tmem + (cc & 1) * 128;
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * KvStage<D>::kPanelBytes + (kk & 3) * 32;
-            umma_bf16_ss(d_tmem, make_sdesc_sw128(q_addr + off, 16, 1024), make_sdesc_sw128(k_addr + off, 16, 1024),
-                         idesc_qk, kk > 0 ? 1u : 0u);
-          }
-          umma_commit(&s_full[cc & 1]);
-          return true;
-        };
-        ok = issue_qk(c);
+          for (int x = 0; x < nx; ++x) issue_qk(x, c % Cfg::kSlots);
+          umma_commit(&empty[c % Cfg::kSlots]);  // K_0 consumed
+        }
         for (int j = 0; ok && j < n; ++j) {
-          const int cj = c + j;
-          if (j + 1 < n && !(ok = issue_qk(cj + 1))) break;
-          if (!mbar_wait(&p_full, cj & 1, &abort_flag, p.err, kDevErrTimeoutMma)) {
+          const int kc = c + 2 * j;  // slot load index of K_j; V_j is kc + 1
+          const bool more = j + 1 < n;
+          if (!slot_wait(kc + 1)) {  // V_j
             ok = false;
             break;
           }
-          if (j == 0 && !mbar_wait(&o_free, (oi & 1) ^ 1, &abort_flag, p.err, kDevErrTimeoutMma)) {
-            ok = false;
-            break;
+          for (int x = 0; x < nx; ++x) {
+            const int tsx = x ? ts1 : ts0, oix = x ? oi1 : oi0;
+            if (!mbar_wait(&p_full[x], tsx & 1, &abort_flag, p.err, kDevErrTimeoutMma) ||
+                (j == 0 && !mbar_wait(&o_free[x], (oix & 1) ^ 1, &abort_flag, p.err, kDevErrTimeoutMma))) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_pv(x, (kc + 1) % Cfg::kSlots, j == 0);
+            if (x) ++ts1; else ++ts0;
+            if (more) {
+              // K_{j+1} is awaited only now, so its load overlaps the softmax of tile A
+              if (x == 0 && !slot_wait(kc + 2)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              issue_qk(x, (kc + 2) % Cfg::kSlots);
+            }
           }
-          tc_fence_after();
-          const int st = cj % Cfg::kStages;
-          const uint32_t v_addr = smem_u32(stages + st * Cfg::kStageBytes);
-#pragma unroll
-          for (int kk = 0; kk < kBN / 16; ++kk) {
-            const uint32_t poff = (kk >> 2) * (kRows * 128) + (kk & 3) * 32;
-            umma_bf16_ss(tmem + Cfg::kOCol, make_sdesc_sw128(p_addr + poff, 16, 1024),
-                         make_sdesc_sw128(v_addr + kk * 2048, KvStage<D>::kPanelBytes, 1024), idesc_pv,
-                         (j > 0 || kk > 0) ? 1u : 0u);
-          }
-          umma_commit(&empty[st]);
-          umma_commit(&o_full);
+          if (!ok) break;
+          umma_commit(&empty[(kc + 1) % Cfg::kSlots]);            // V_j consumed
+          if (more) umma_commit(&empty[(kc + 2) % Cfg::kSlots]);  // K_{j+1} consumed
         }
       }
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-      if (n > 0) ++oi;
-      c += n;
+      ts0 = __shfl_sync(0xffffffffu, ts0, 0);
+      ts1 = __shfl_sync(0xffffffffu, ts1, 0);
+      if (n > 0) {
+        ++oi0;
+        if (nx == 2) ++oi1;
+      }
+      c += 2 * n;
       __syncwarp();
       if (lane == 0) mbar_arrive(&item_empty[slot]);
     }
   } else {
     // ------------------------------------------------------------ softmax / epilogue
-    const int quad = warp & 3;
-    const int r = quad * 32 + lane;  // packed row of the tile == TMEM lane
+    const int x = (warp - 2) >> 2;   // q tile of this warpgroup
+    const int quad = warp & 3;       // TMEM lane quadrant this warp may access
+    const int r = quad * 32 + lane;  // row of the q tile == TMEM lane
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
-    int c = 0;
+    const uint32_t s_col = lane_base + s_col_of(x);
+    const uint32_t o_col = lane_base + o_col_of(x);
+    uint8_t* q_tile = q_smem + x * Cfg::kQBytes;
+    uint8_t* p_row = p_smem + x * Cfg::kPBytes + r * 128;
+    int ts = 0;  // kv tiles processed by this q tile (phase counter)
     for (int k = 0;; ++k) {
       const int slot = k & 1;
       if (!mbar_wait(&item_full[slot], (k >> 1) & 1, &abort_flag, p.err, kDevErrTimeoutSoftmax)) break;
@@ -168,8 +214,9 @@ __global__ void __launch_bounds__(192, 1)
       if (idx >= p.num_items) break;
       const Work w = get_work(p, idx);
       const int n = w.tile_end - w.tile_begin;
-      const bool row_valid = r < w.nrows;
-      const int R = w.row0 + r;
+      const bool tile_active = (x == 0) || (w.nrows > kRows);
+      const int R = w.row0 + x * kRows + r;
+      const bool row_valid = (x * kRows + r) < w.nrows;
       const int tok = w.q0 + (row_valid ? R / p.group : 0);
       const int qh = w.h * p.group + R % p.group;
 
@@ -181,120 +228,136 @@ __global__ void __launch_bounds__(192, 1)
           uint4 val = make_uint4(0, 0, 0, 0);
           if (row_valid) val = __ldg(reinterpret_cast<const uint4*>(src + u * 8));
           const int ch = u >> 3, uu = u & 7;
-          *reinterpret_cast<uint4*>(q_smem + ch * (kRows * 128) + r * 128 + ((uu ^ (r & 7)) << 4)) = val;
+          *reinterpret_cast<uint4*>(q_tile + ch * (kRows * 128) + r * 128 + ((uu ^ (r & 7)) << 4)) = val;
         }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&q_full[slot]);
       }
+      if (!tile_active) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&item_empty[slot]);
+        continue;
+      }
       int lo = 1, hi = 0;
       if (row_valid) visible_range(p, R / p.group, w.q_len, w.kv_len, lo, hi);
 
-      float m = -INFINITY, l = 0.f;
+      float m_ref = -INFINITY;  // max the P values and O are referenced to (scaled log2 domain)
+      float l = 0.f;
       bool ok = true;
       for (int j = 0; j < n; ++j) {
-        const int cj = c + j;
-        if (!mbar_wait(&s_full[cj & 1], (cj >> 1) & 1, &abort_flag, p.err, kDevErrTimeoutSoftmax)) {
+        if (!mbar_wait(&s_full[x], ts & 1, &abort_flag, p.err, kDevErrTimeoutSoftmax)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        float s[128];
+        const int base = (w.tile_begin + j) * kBN;
+        const bool full_tile = __all_sync(0xffffffffu, (base >= lo) && (base + kBN - 1 <= hi));
+        // pass 1: row max of the visible scores
+        float tmax = -INFINITY;
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) {
           float t[32];
-          tmem_ld32(lane_base + (cj & 1) * 128 + q4 * 32, t);
+          tmem_ld32(s_col + q4 * 32, t);
+          tmem_wait_ld();
+          if (full_tile) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) s[q4 * 32 + i] = t[i];
-        }
-        tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&s_free[cj & 1]);
-
-        const int base = (w.tile_begin + j) * kBN;
-        float tmax = -INFINITY;
-        const bool full_tile = (base >= lo) && (base + kBN - 1 <= hi);
-        if (__all_sync(0xffffffffu, full_tile)) {
+            for (int i = 0; i < 32; ++i) tmax = fmaxf(tmax, t[i]);
+          } else {
 #pragma unroll
-          for (int i = 0; i < 128; ++i) {
-            s[i] *= p.scale_log2;
-            tmax = fmaxf(tmax, s[i]);
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 128; ++i) {
-            const int pos = base + i;
-            s[i] = (pos >= lo && pos <= hi) ? s[i] * p.scale_log2 : -INFINITY;
-            tmax = fmaxf(tmax, s[i]);
+            for (int i = 0; i < 32; ++i) {
+              const int pos = base + q4 * 32 + i;
+              tmax = fmaxf(tmax, (pos >= lo && pos <= hi) ? t[i] : -INFINITY);
+            }
           }
         }
-        const float mn = fmaxf(m, tmax);
-        const float alpha = (m == -INFINITY) ? 1.f : ex2_approx(m - mn);
-        // previous P.V must be complete before O is rescaled or P is overwritten
+        tmax *= p.scale_log2;
+        // reference max: moves only when the new max exceeds it by the threshold
+        float alpha = 1.f;
+        bool rescale = false;
+        if (tmax > m_ref + kRescaleThreshold || (m_ref == -INFINITY && tmax > -INFINITY)) {
+          if (m_ref != -INFINITY) {
+            alpha = ex2_approx(m_ref - tmax);
+            rescale = true;
+          }
+          m_ref = tmax;
+        }
+        // the previous P.V of this q tile must be complete before O is rescaled or P rewritten
         if (j > 0) {
-          if (!mbar_wait(&o_full, (cj - 1) & 1, &abort_flag, p.err, kDevErrTimeoutSoftmax)) {
+          if (!mbar_wait(&o_full[x], (ts - 1) & 1, &abort_flag, p.err, kDevErrTimeoutSoftmax)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const bool need = alpha != 1.f;
-          if (__any_sync(0xffffffffu, need)) {
-#pragma unroll
+          if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
             for (int cc = 0; cc < D / 32; ++cc) {
               float t[32];
-              tmem_ld32(lane_base + Cfg::kOCol + cc * 32, t);
+              tmem_ld32(o_col + cc * 32, t);
               tmem_wait_ld();
 #pragma unroll
               for (int i = 0; i < 32; ++i) t[i] *= alpha;
-              tmem_st32(lane_base + Cfg::kOCol + cc * 32, t);
+              tmem_st32(o_col + cc * 32, t);
             }
             tmem_wait_st();
           }
         }
-        const float ms = (mn == -INFINITY) ? 0.f : mn;
+        l *= alpha;
+        // pass 2: P = 2^(s*scale - m_ref) -> bf16 -> shared memory, row sum
+        const float ms = (m_ref == -INFINITY) ? 0.f : m_ref;
         float rs = 0.f;
-        uint8_t* prow = p_smem + r * 128;
 #pragma unroll
-        for (int u = 0; u < 16; ++u) {
-          uint32_t pk[4];
+        for (int q4 = 0; q4 < 4; ++q4) {
+          float t[32];
+          tmem_ld32(s_col + q4 * 32, t);
+          tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float p0 = ex2_approx(s[u * 8 + 2 * e] - ms);
-            const float p1 = ex2_approx(s[u * 8 + 2 * e + 1] - ms);
-            rs += p0 + p1;
-            __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
-            pk[e] = *reinterpret_cast<uint32_t*>(&h2);
+          for (int v4 = 0; v4 < 4; ++v4) {
+            uint32_t pk[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int i0 = v4 * 8 + 2 * e;
+              const int pos = base + q4 * 32 + i0;
+              float a = t[i0] * p.scale_log2 - ms;
+              float b = t[i0 + 1] * p.scale_log2 - ms;
+              if (!full_tile) {
+                a = (pos >= lo && pos <= hi) ? a : -INFINITY;
+                b = (pos + 1 >= lo && pos + 1 <= hi) ? b : -INFINITY;
+              }
+              const float p0 = ex2_approx(a), p1 = ex2_approx(b);
+              rs += p0 + p1;
+              __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
+              pk[e] = *reinterpret_cast<uint32_t*>(&h2);
+            }
+            const int u = q4 * 4 + v4;  // 16-byte unit of the 256-byte row
+            const int ch = u >> 3, uu = u & 7;
+            *reinterpret_cast<uint4*>(p_row + ch * (kRows * 128) + ((uu ^ (r & 7)) << 4)) =
+                make_uint4(pk[0], pk[1], pk[2], pk[3]);
           }
-          const int ch = u >> 3, uu = u & 7;
-          *reinterpret_cast<uint4*>(prow + ch * (kRows * 128) + ((uu ^ (r & 7)) << 4)) =
-              make_uint4(pk[0], pk[1], pk[2], pk[3]);
         }
-        l = l * alpha + rs;
-        m = mn;
+        l += rs;
+        ++ts;
         fence_proxy_async_smem();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&p_full);
+        if (lane == 0) mbar_arrive(&p_full[x]);
       }
       if (!ok) break;
       if (n > 0) {
-        const int cl = c + n - 1;
-        if (!mbar_wait(&o_full, cl & 1, &abort_flag, p.err, kDevErrTimeoutSoftmax)) break;
+        if (!mbar_wait(&o_full[x], (ts - 1) & 1, &abort_flag, p.err, kDevErrTimeoutSoftmax)) break;
         tc_fence_after();
       }
-      c += n;
 
       // epilogue: O / l -> out (single split) or the fp32 partial buffers
       const bool direct = (w.nsplits == 1);
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      const float lse2 = l > 0.f ? m + lg2_approx(l) : -INFINITY;
+      const float lse2 = l > 0.f ? m_ref + lg2_approx(l) : -INFINITY;
       const int64_t prow_idx = ((int64_t)w.split * p.total_q + tok) * p.hq + qh;
-#pragma unroll
+#pragma unroll 1
       for (int cc = 0; cc < D / 32; ++cc) {
         float t[32];
         if (n > 0) {
-          tmem_ld32(lane_base + Cfg::kOCol + cc * 32, t);
+          tmem_ld32(o_col + cc * 32, t);
           tmem_wait_ld();
         } else {
 #pragma unroll
@@ -332,7 +395,7 @@ __global__ void __launch_bounds__(192, 1)
       if (n > 0) {
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&o_free);
+        if (lane == 0) mbar_arrive(&o_free[x]);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&item_empty[slot]);
@@ -371,7 +434,7 @@ cudaError_t launch_prefill(const FwdParams& p, const KvMaps& maps, int grid, cud
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
-  prefill_kernel<D><<<grid, 192, PrefillCfg<D>::kDynBytes, s>>>(p, maps);
+  prefill_kernel<D><<<grid, 320, PrefillCfg<D>::kDynBytes, s>>>(p, maps);
   return cudaGetLastError();
 }
 

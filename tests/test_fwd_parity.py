@@ -243,6 +243,6 @@ def test_plan_decode_vs_prefill_selection():
     c3 = baseline_config("C3").to("cuda")
     p = faf.plan(c3.q, c3.k_cache, c3.v_cache, c3.cu_seqlens_q, c3.seqused_k, c3.block_table, c3.max_seqlen_q,
                  c3.max_seqlen_k, True)
-    assert p["kernel"] == 1 and p["rows_per_tile"] == 128
+    assert p["kernel"] == 1 and p["rows_per_tile"] in (128, 256)
     assert p["grid"] <= torch.cuda.get_device_properties(0).multi_processor_count
     assert math.isfinite(p["workspace_bytes"])

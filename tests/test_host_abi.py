@@ -114,7 +114,10 @@ def test_plan_without_gpu_uses_b200_sm_count():
     assert info.grid == min(info.num_items, 148)
     p.max_seqlen_q = 128
     assert _lib.load().tfa_plan(ctypes.byref(p), -1, ctypes.byref(info)) == 0
-    assert info.kernel == 1 and info.rows_per_tile == 128 and info.q_tiles == 7
+    assert info.kernel == 1 and info.rows_per_tile == 128 and info.q_tiles == 7  # few items: 128-row items
+    p.batch, p.total_q, p.max_seqlen_q = 64, 64 * 4096, 4096
+    assert _lib.load().tfa_plan(ctypes.byref(p), -1, ctypes.byref(info)) == 0
+    assert info.rows_per_tile == 256 and info.q_tiles == 112
 
 
 def test_workspace_size_grows_with_splits():
