@@ -2,6 +2,8 @@
 // split-KV planning, TMA descriptor encoding and kernel launches. Host code only.
 #include <cmath>
 #include <cstdint>
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
 
 #include "../../include/tfa.h"
@@ -276,7 +278,10 @@ int fwd_impl(const tfa_fwd_params* a, void* workspace, size_t workspace_bytes, v
     e = pl.kernel == 0 ? launch_decode<64>(p, maps, pl.grid, s) : launch_prefill<64>(p, maps, pl.grid, s);
   else
     e = pl.kernel == 0 ? launch_decode<128>(p, maps, pl.grid, s) : launch_prefill<128>(p, maps, pl.grid, s);
-  if (e != cudaSuccess) return TFA_ERR_CUDA;
+  if (e != cudaSuccess) {
+    if (std::getenv("TFA_DEBUG")) std::fprintf(stderr, "tfa_fwd: launch failed: %s\n", cudaGetErrorString(e));
+    return TFA_ERR_CUDA;
+  }
   if (ev_end && cudaEventRecord(reinterpret_cast<cudaEvent_t>(ev_end), s) != cudaSuccess) return TFA_ERR_CUDA;
   if (pl.combine) {
     e = a->head_dim == 64 ? launch_combine<64>(p, s) : launch_combine<128>(p, s);

@@ -13,9 +13,8 @@
 // Per kv tile and q tile:
 //   S[128 x 128] = Q[128 x D] . K^T   (tcgen05, A = Q K-major, B = K K-major), S in TMEM
 //   O[128 x D]  += P[128 x 128] . V   (tcgen05, A = P K-major, B = V MN-major), O in TMEM
-// Softmax threads own one row each (TMEM lane = row): pass 1 reads S for the row max,
-// pass 2 reads it again to form P (bf16, written to swizzled shared memory) and the row
-// sum. O is rescaled in TMEM only when a row's max grows by more than 2^8 over the max
+// Softmax threads own one row each (TMEM lane = row) and hold its 128 scores in
+// registers (one TMEM load per tile); P goes to swizzled shared memory as bf16. O is rescaled in TMEM only when a row's max grows by more than 2^8 over the max
 // its P values are referenced to (values of P stay <= 256, far inside bf16/fp32 range),
 // so most tiles need no O round trip.
 //
@@ -253,22 +252,18 @@ __global__ void __launch_bounds__(320, 1)
         tc_fence_after();
         const int base = (w.tile_begin + j) * kBN;
         const bool full_tile = __all_sync(0xffffffffu, (base >= lo) && (base + kBN - 1 <= hi));
-        // pass 1: row max of the visible scores
+        // the whole 128-score row in registers, one TMEM load
+        float sv[128];
+        tmem_ld128_sync(s_col, sv);
         float tmax = -INFINITY;
+        if (full_tile) {
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          float t[32];
-          tmem_ld32(s_col + q4 * 32, t);
-          tmem_wait_ld();
-          if (full_tile) {
+          for (int i = 0; i < 128; ++i) tmax = fmaxf(tmax, sv[i]);
+        } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) tmax = fmaxf(tmax, t[i]);
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const int pos = base + q4 * 32 + i;
-              tmax = fmaxf(tmax, (pos >= lo && pos <= hi) ? t[i] : -INFINITY);
-            }
+          for (int i = 0; i < 128; ++i) {
+            sv[i] = (base + i >= lo && base + i <= hi) ? sv[i] : -INFINITY;
+            tmax = fmaxf(tmax, sv[i]);
           }
         }
         tmax *= p.scale_log2;
@@ -303,37 +298,23 @@ __global__ void __launch_bounds__(320, 1)
           }
         }
         l *= alpha;
-        // pass 2: P = 2^(s*scale - m_ref) -> bf16 -> shared memory, row sum
+        // P = 2^(s*scale - m_ref) -> bf16 -> shared memory, row sum
         const float ms = (m_ref == -INFINITY) ? 0.f : m_ref;
         float rs = 0.f;
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          float t[32];
-          tmem_ld32(s_col + q4 * 32, t);
-          tmem_wait_ld();
+        for (int u = 0; u < 16; ++u) {  // 16-byte unit of the 256-byte row
+          uint32_t pk[4];
 #pragma unroll
-          for (int v4 = 0; v4 < 4; ++v4) {
-            uint32_t pk[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int i0 = v4 * 8 + 2 * e;
-              const int pos = base + q4 * 32 + i0;
-              float a = t[i0] * p.scale_log2 - ms;
-              float b = t[i0 + 1] * p.scale_log2 - ms;
-              if (!full_tile) {
-                a = (pos >= lo && pos <= hi) ? a : -INFINITY;
-                b = (pos + 1 >= lo && pos + 1 <= hi) ? b : -INFINITY;
-              }
-              const float p0 = ex2_approx(a), p1 = ex2_approx(b);
-              rs += p0 + p1;
-              __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
-              pk[e] = *reinterpret_cast<uint32_t*>(&h2);
-            }
-            const int u = q4 * 4 + v4;  // 16-byte unit of the 256-byte row
-            const int ch = u >> 3, uu = u & 7;
-            *reinterpret_cast<uint4*>(p_row + ch * (kRows * 128) + ((uu ^ (r & 7)) << 4)) =
-                make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          for (int e = 0; e < 4; ++e) {
+            const float p0 = ex2_approx(fmaf(sv[u * 8 + 2 * e], p.scale_log2, -ms));
+            const float p1 = ex2_approx(fmaf(sv[u * 8 + 2 * e + 1], p.scale_log2, -ms));
+            rs += p0 + p1;
+            __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
+            pk[e] = *reinterpret_cast<uint32_t*>(&h2);
           }
+          const int ch = u >> 3, uu = u & 7;
+          *reinterpret_cast<uint4*>(p_row + ch * (kRows * 128) + ((uu ^ (r & 7)) << 4)) =
+              make_uint4(pk[0], pk[1], pk[2], pk[3]);
         }
         l += rs;
         ++ts;

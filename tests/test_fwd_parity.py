@@ -81,6 +81,22 @@ def test_long_prefill_d128_gqa():
     assert_parity(case)
 
 
+@pytest.mark.parametrize(
+    "q_lens, hq, hkv, hd",
+    [([1024] * 6, 14, 2, 64), ([512] * 7 + [300], 32, 8, 128), ([700, 1024, 33, 513] * 2, 16, 4, 128)],
+    ids=["d64_g7", "d128_g4", "d128_g4_ragged"],
+)
+def test_two_tile_prefill_items(q_lens, hq, hkv, hd):
+    """Large prefill batches use 256-row items (two q tiles per CTA)."""
+    case = reference_case(q_lens, num_heads=hq, num_kv_heads=hkv, head_dim=hd, causal=True, block_size=16,
+                          seed=len(q_lens) + hd)
+    c = case.to("cuda")
+    p = faf.plan(c.q, c.k_cache, c.v_cache, c.cu_seqlens_q, c.seqused_k, c.block_table, c.max_seqlen_q,
+                 c.max_seqlen_k, True)
+    assert p["kernel"] == 1 and p["rows_per_tile"] == 256
+    assert_parity(case)
+
+
 def test_c5_reduced_batch_full_lengths():
     case = baseline_config("C5", batch=12, num_blocks=40000)
     assert_parity(case)
