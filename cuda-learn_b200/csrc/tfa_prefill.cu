@@ -255,17 +255,17 @@ __global__ void __launch_bounds__(320, 1)
         // the whole 128-score row in registers, one TMEM load
         float sv[128];
         tmem_ld128_sync(s_col, sv);
-        float tmax = -INFINITY;
-        if (full_tile) {
+        // row max over 8 independent partial maxima (short dependency chains)
+        float m8[8];
 #pragma unroll
-          for (int i = 0; i < 128; ++i) tmax = fmaxf(tmax, sv[i]);
-        } else {
+        for (int e = 0; e < 8; ++e) m8[e] = -INFINITY;
+        if (!full_tile) {
 #pragma unroll
-          for (int i = 0; i < 128; ++i) {
-            sv[i] = (base + i >= lo && base + i <= hi) ? sv[i] : -INFINITY;
-            tmax = fmaxf(tmax, sv[i]);
-          }
+          for (int i = 0; i < 128; ++i) sv[i] = (base + i >= lo && base + i <= hi) ? sv[i] : -INFINITY;
         }
+#pragma unroll
+        for (int i = 0; i < 128; ++i) m8[i & 7] = fmaxf(m8[i & 7], sv[i]);
+        float tmax = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
         tmax *= p.scale_log2;
         // reference max: moves only when the new max exceeds it by the threshold
         float alpha = 1.f;
@@ -300,7 +300,7 @@ __global__ void __launch_bounds__(320, 1)
         l *= alpha;
         // P = 2^(s*scale - m_ref) -> bf16 -> shared memory, row sum
         const float ms = (m_ref == -INFINITY) ? 0.f : m_ref;
-        float rs = 0.f;
+        float rs8[4] = {0.f, 0.f, 0.f, 0.f};  // partial row sums
 #pragma unroll
         for (int u = 0; u < 16; ++u) {  // 16-byte unit of the 256-byte row
           uint32_t pk[4];
@@ -308,7 +308,7 @@ __global__ void __launch_bounds__(320, 1)
           for (int e = 0; e < 4; ++e) {
             const float p0 = ex2_approx(fmaf(sv[u * 8 + 2 * e], p.scale_log2, -ms));
             const float p1 = ex2_approx(fmaf(sv[u * 8 + 2 * e + 1], p.scale_log2, -ms));
-            rs += p0 + p1;
+            rs8[e] += p0 + p1;
             __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
             pk[e] = *reinterpret_cast<uint32_t*>(&h2);
           }
@@ -316,7 +316,7 @@ __global__ void __launch_bounds__(320, 1)
           *reinterpret_cast<uint4*>(p_row + ch * (kRows * 128) + ((uu ^ (r & 7)) << 4)) =
               make_uint4(pk[0], pk[1], pk[2], pk[3]);
         }
-        l += rs;
+        l += (rs8[0] + rs8[1]) + (rs8[2] + rs8[3]);
         ++ts;
         fence_proxy_async_smem();
         tc_fence_before();
