@@ -12,9 +12,11 @@
 //
 // Per kv tile and q tile:
 //   S[128 x 128] = Q[128 x D] . K^T   (tcgen05, A = Q K-major, B = K K-major), S in TMEM
-//   O[128 x D]  += P[128 x 128] . V   (tcgen05, A = P K-major, B = V MN-major), O in TMEM
+//   O[128 x D]  += P[128 x 128] . V   (tcgen05, A = P from TMEM, B = V MN-major), O in TMEM
 // Softmax threads own one row each (TMEM lane = row) and hold its 128 scores in
-// registers (one TMEM load per tile); P goes to swizzled shared memory as bf16. O is rescaled in TMEM only when a row's max grows by more than 2^8 over the max
+// registers (one TMEM load per tile); P is stored back as bf16 pairs over the first 64
+// columns of the same S region and read from there by the P.V MMA, so P never touches
+// shared memory (whose bandwidth the MMAs' smem operands and the TMA fills already use). O is rescaled in TMEM only when a row's max grows by more than 2^8 over the max
 // its P values are referenced to (values of P stay <= 256, far inside bf16/fp32 range),
 // so most tiles need no O round trip.
 //
@@ -28,6 +30,13 @@ namespace tfa {
 
 namespace {
 
+#ifdef TFA_PROFILE
+__device__ unsigned long long g_prefill_prof[1024 * 16];
+#define PROF_WAIT(cat, expr) ([&]() { const long long _t0 = clock64(); const bool _r = (expr); prof[cat] += clock64() - _t0; return _r; }())
+#else
+#define PROF_WAIT(cat, expr) (expr)
+#endif
+
 constexpr int kRows = 128;                // rows per q tile
 constexpr float kRescaleThreshold = 8.f;  // log2 units
 
@@ -35,13 +44,11 @@ template <int D>
 struct PrefillCfg {
   static constexpr int kPanels = D / 64;
   static constexpr int kSlotBytes = KvStage<D>::kTensorBytes;  // one K or V tile
-  static constexpr int kSlots = (D == 128) ? 3 : 6;
+  static constexpr int kSlots = (D == 128) ? 5 : 10;
   static constexpr int kQBytes = kPanels * kRows * 128;        // per q tile
-  static constexpr int kPBytes = 2 * kRows * 128;              // 128 rows x 128 tokens bf16
   static constexpr int kQOff = kSlots * kSlotBytes;
-  static constexpr int kPOff = kQOff + 2 * kQBytes;
-  static constexpr int kDynBytes = kPOff + 2 * kPBytes + 1024;
-  static constexpr uint32_t kTmemCols = 512;                   // S_A, S_B, O_A, O_B
+  static constexpr int kDynBytes = kQOff + 2 * kQBytes + 1024;
+  static constexpr uint32_t kTmemCols = 512;                   // S_A, S_B (P aliases their first 64), O_A, O_B
 };
 
 __device__ __forceinline__ uint32_t s_col_of(int x) { return x == 0 ? 0u : 128u; }
@@ -55,7 +62,6 @@ __global__ void __launch_bounds__(320, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dyn_smem) + 1023) & ~uintptr_t(1023));
   uint8_t* slots = smem;
   uint8_t* q_smem = smem + Cfg::kQOff;
-  uint8_t* p_smem = smem + Cfg::kPOff;
 
   __shared__ uint64_t full[Cfg::kSlots], empty[Cfg::kSlots];
   __shared__ uint64_t s_full[2], p_full[2], o_full[2], o_free[2];
@@ -67,6 +73,10 @@ __global__ void __launch_bounds__(320, 1)
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
+#ifdef TFA_PROFILE
+  unsigned long long prof[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  const long long prof_start = clock64();
+#endif
 
   if (tid == 0) {
     for (int i = 0; i < Cfg::kSlots; ++i) {
@@ -104,13 +114,12 @@ __global__ void __launch_bounds__(320, 1)
     const uint32_t idesc_qk = make_idesc_bf16_f32(128, 128, false, false);
     const uint32_t idesc_pv = make_idesc_bf16_f32(128, D, false, true);
     const uint32_t q_addr = smem_u32(q_smem);
-    const uint32_t p_addr = smem_u32(p_smem);
     int c = 0;           // slot loads consumed (2 per kv tile)
     int ts0 = 0, ts1 = 0;  // kv tiles processed per q tile (phase counters)
     int oi0 = 0, oi1 = 0;  // non-empty items per q tile
     bool ok = true;
     auto slot_wait = [&](int cc) -> bool {
-      return mbar_wait(&full[cc % Cfg::kSlots], (cc / Cfg::kSlots) & 1, &abort_flag, p.err, kDevErrTimeoutMma);
+      return PROF_WAIT(0, mbar_wait(&full[cc % Cfg::kSlots], (cc / Cfg::kSlots) & 1, &abort_flag, p.err, kDevErrTimeoutMma));
     };
     auto issue_qk = [&](int x, int kslot) {
       const uint32_t k_addr = smem_u32(slots + kslot * Cfg::kSlotBytes);
@@ -125,11 +134,10 @@ __global__ void __launch_bounds__(320, 1)
     };
     auto issue_pv = [&](int x, int vslot, bool first) {
       const uint32_t v_addr = smem_u32(slots + vslot * Cfg::kSlotBytes);
-      const uint32_t px = p_addr + x * Cfg::kPBytes;
+      const uint32_t p_tmem = tmem + s_col_of(x);  // P (bf16 pairs) over the first 64 S columns
 #pragma unroll
       for (int kk = 0; kk < kBN / 16; ++kk) {
-        const uint32_t poff = (kk >> 2) * (kRows * 128) + (kk & 3) * 32;
-        umma_bf16_ss(tmem + o_col_of(x), make_sdesc_sw128(px + poff, 16, 1024),
+        umma_bf16_ts(tmem + o_col_of(x), p_tmem + kk * 8,
                      make_sdesc_sw128(v_addr + kk * 2048, KvStage<D>::kPanelBytes, 1024), idesc_pv,
                      (!first || kk > 0) ? 1u : 0u);
       }
@@ -137,13 +145,13 @@ __global__ void __launch_bounds__(320, 1)
     };
     for (int k = 0; ok; ++k) {
       const int slot = k & 1;
-      if (!mbar_wait(&item_full[slot], (k >> 1) & 1, &abort_flag, p.err, kDevErrTimeoutMma)) break;
+      if (!PROF_WAIT(3, mbar_wait(&item_full[slot], (k >> 1) & 1, &abort_flag, p.err, kDevErrTimeoutMma))) break;
       const int idx = item_slot[slot];
       if (idx >= p.num_items) break;
       const Work w = get_work(p, idx);
       const int n = w.tile_end - w.tile_begin;
       const int nx = w.nrows > kRows ? 2 : 1;  // q tiles with rows
-      if (!mbar_wait(&q_full[slot], (k >> 1) & 1, &abort_flag, p.err, kDevErrTimeoutMma)) break;
+      if (!PROF_WAIT(3, mbar_wait(&q_full[slot], (k >> 1) & 1, &abort_flag, p.err, kDevErrTimeoutMma))) break;
       if (lane == 0 && n > 0) {
         // QK of the first kv tile for both q tiles
         ok = slot_wait(c);
@@ -161,8 +169,8 @@ __global__ void __launch_bounds__(320, 1)
           }
           for (int x = 0; x < nx; ++x) {
             const int tsx = x ? ts1 : ts0, oix = x ? oi1 : oi0;
-            if (!mbar_wait(&p_full[x], tsx & 1, &abort_flag, p.err, kDevErrTimeoutMma) ||
-                (j == 0 && !mbar_wait(&o_free[x], (oix & 1) ^ 1, &abort_flag, p.err, kDevErrTimeoutMma))) {
+            if (!PROF_WAIT(1, mbar_wait(&p_full[x], tsx & 1, &abort_flag, p.err, kDevErrTimeoutMma)) ||
+                (j == 0 && !PROF_WAIT(2, mbar_wait(&o_free[x], (oix & 1) ^ 1, &abort_flag, p.err, kDevErrTimeoutMma)))) {
               ok = false;
               break;
             }
@@ -170,8 +178,11 @@ __global__ void __launch_bounds__(320, 1)
             issue_pv(x, (kc + 1) % Cfg::kSlots, j == 0);
             if (x) ++ts1; else ++ts0;
             if (more) {
-              // K_{j+1} is awaited only now, so its load overlaps the softmax of tile A
-              if (x == 0 && !slot_wait(kc + 2)) {
+              // QK(j+1) overwrites S, whose first columns hold the P this P.V reads:
+              // wait for the P.V to finish. K_{j+1} is awaited only now, so its load
+              // overlaps the softmax of tile A.
+              if (!mbar_wait(&o_full[x], ((x ? ts1 : ts0) - 1) & 1, &abort_flag, p.err, kDevErrTimeoutMma) ||
+                  (x == 0 && !slot_wait(kc + 2))) {
                 ok = false;
                 break;
               }
@@ -204,11 +215,10 @@ __global__ void __launch_bounds__(320, 1)
     const uint32_t s_col = lane_base + s_col_of(x);
     const uint32_t o_col = lane_base + o_col_of(x);
     uint8_t* q_tile = q_smem + x * Cfg::kQBytes;
-    uint8_t* p_row = p_smem + x * Cfg::kPBytes + r * 128;
     int ts = 0;  // kv tiles processed by this q tile (phase counter)
     for (int k = 0;; ++k) {
       const int slot = k & 1;
-      if (!mbar_wait(&item_full[slot], (k >> 1) & 1, &abort_flag, p.err, kDevErrTimeoutSoftmax)) break;
+      if (!PROF_WAIT(3, mbar_wait(&item_full[slot], (k >> 1) & 1, &abort_flag, p.err, kDevErrTimeoutSoftmax))) break;
       const int idx = item_slot[slot];
       if (idx >= p.num_items) break;
       const Work w = get_work(p, idx);
@@ -245,7 +255,7 @@ __global__ void __launch_bounds__(320, 1)
       float l = 0.f;
       bool ok = true;
       for (int j = 0; j < n; ++j) {
-        if (!mbar_wait(&s_full[x], ts & 1, &abort_flag, p.err, kDevErrTimeoutSoftmax)) {
+        if (!PROF_WAIT(0, mbar_wait(&s_full[x], ts & 1, &abort_flag, p.err, kDevErrTimeoutSoftmax))) {
           ok = false;
           break;
         }
@@ -279,7 +289,7 @@ __global__ void __launch_bounds__(320, 1)
         }
         // the previous P.V of this q tile must be complete before O is rescaled or P rewritten
         if (j > 0) {
-          if (!mbar_wait(&o_full[x], (ts - 1) & 1, &abort_flag, p.err, kDevErrTimeoutSoftmax)) {
+          if (!PROF_WAIT(1, mbar_wait(&o_full[x], (ts - 1) & 1, &abort_flag, p.err, kDevErrTimeoutSoftmax))) {
             ok = false;
             break;
           }
@@ -298,34 +308,33 @@ __global__ void __launch_bounds__(320, 1)
           }
         }
         l *= alpha;
-        // P = 2^(s*scale - m_ref) -> bf16 -> shared memory, row sum
+        // P = 2^(s*scale - m_ref) -> bf16 pairs -> TMEM (over the S columns), row sum
         const float ms = (m_ref == -INFINITY) ? 0.f : m_ref;
         float rs8[4] = {0.f, 0.f, 0.f, 0.f};  // partial row sums
 #pragma unroll
-        for (int u = 0; u < 16; ++u) {  // 16-byte unit of the 256-byte row
-          uint32_t pk[4];
+        for (int h = 0; h < 2; ++h) {
+          float pk[32];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float p0 = ex2_approx(fmaf(sv[u * 8 + 2 * e], p.scale_log2, -ms));
-            const float p1 = ex2_approx(fmaf(sv[u * 8 + 2 * e + 1], p.scale_log2, -ms));
-            rs8[e] += p0 + p1;
+          for (int c = 0; c < 32; ++c) {
+            const int i0 = h * 64 + 2 * c;
+            const float p0 = ex2_approx(fmaf(sv[i0], p.scale_log2, -ms));
+            const float p1 = ex2_approx(fmaf(sv[i0 + 1], p.scale_log2, -ms));
+            rs8[c & 3] += p0 + p1;
             __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
-            pk[e] = *reinterpret_cast<uint32_t*>(&h2);
+            pk[c] = __uint_as_float(*reinterpret_cast<uint32_t*>(&h2));
           }
-          const int ch = u >> 3, uu = u & 7;
-          *reinterpret_cast<uint4*>(p_row + ch * (kRows * 128) + ((uu ^ (r & 7)) << 4)) =
-              make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          tmem_st32(s_col + h * 32, pk);
         }
+        tmem_wait_st();
         l += (rs8[0] + rs8[1]) + (rs8[2] + rs8[3]);
         ++ts;
-        fence_proxy_async_smem();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[x]);
       }
       if (!ok) break;
       if (n > 0) {
-        if (!mbar_wait(&o_full[x], (ts - 1) & 1, &abort_flag, p.err, kDevErrTimeoutSoftmax)) break;
+        if (!PROF_WAIT(2, mbar_wait(&o_full[x], (ts - 1) & 1, &abort_flag, p.err, kDevErrTimeoutSoftmax))) break;
         tc_fence_after();
       }
 
@@ -383,6 +392,13 @@ __global__ void __launch_bounds__(320, 1)
     }
   }
 
+#ifdef TFA_PROFILE
+  prof[4] = clock64() - prof_start;
+  if (lane == 0 && (warp == 1 || warp == 2 || warp == 6) && blockIdx.x < 1024) {
+    const int base_idx = blockIdx.x * 16 + (warp == 1 ? 0 : (warp == 2 ? 5 : 10));
+    for (int i = 0; i < 5; ++i) g_prefill_prof[base_idx + i] = prof[i];
+  }
+#endif
   if (abort_flag && warp == 0) {
     const uint64_t t0 = global_timer_ns();
     while (global_timer_ns() - t0 < 100000ull) __nanosleep(1000);
@@ -418,6 +434,12 @@ cudaError_t launch_prefill(const FwdParams& p, const KvMaps& maps, int grid, cud
   prefill_kernel<D><<<grid, 320, PrefillCfg<D>::kDynBytes, s>>>(p, maps);
   return cudaGetLastError();
 }
+
+#ifdef TFA_PROFILE
+extern "C" __attribute__((visibility("default"))) int tfa_prefill_prof_read(unsigned long long* host) {
+  return (int)cudaMemcpyFromSymbol(host, g_prefill_prof, sizeof(g_prefill_prof));
+}
+#endif
 
 template int prefill_smem_bytes<64>();
 template int prefill_smem_bytes<128>();
