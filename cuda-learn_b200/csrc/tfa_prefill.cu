@@ -265,7 +265,7 @@ __global__ void __launch_bounds__(320, 1)
         // the whole 128-score row in registers, one TMEM load
         float sv[128];
         tmem_ld128_sync(s_col, sv);
-        // row max over 8 independent partial maxima (short dependency chains)
+        // row max over 8 independent partial maxima, three-input max (short chains)
         float m8[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) m8[e] = -INFINITY;
@@ -274,8 +274,8 @@ __global__ void __launch_bounds__(320, 1)
           for (int i = 0; i < 128; ++i) sv[i] = (base + i >= lo && base + i <= hi) ? sv[i] : -INFINITY;
         }
 #pragma unroll
-        for (int i = 0; i < 128; ++i) m8[i & 7] = fmaxf(m8[i & 7], sv[i]);
-        float tmax = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+        for (int i = 0; i < 64; ++i) m8[i & 7] = fmax3(m8[i & 7], sv[2 * i], sv[2 * i + 1]);
+        float tmax = fmaxf(fmax3(m8[0], m8[1], m8[2]), fmax3(fmax3(m8[3], m8[4], m8[5]), m8[6], m8[7]));
         tmax *= p.scale_log2;
         // reference max: moves only when the new max exceeds it by the threshold
         float alpha = 1.f;
@@ -310,23 +310,29 @@ __global__ void __launch_bounds__(320, 1)
         l *= alpha;
         // P = 2^(s*scale - m_ref) -> bf16 pairs -> TMEM (over the S columns), row sum
         const float ms = (m_ref == -INFINITY) ? 0.f : m_ref;
-        float rs8[4] = {0.f, 0.f, 0.f, 0.f};  // partial row sums
+        const uint64_t scale2 = f2_pack(p.scale_log2, p.scale_log2);
+        const uint64_t neg_ms2 = f2_pack(-ms, -ms);
+        uint64_t rs2[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};  // packed partial row sums
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           float pk[32];
 #pragma unroll
           for (int c = 0; c < 32; ++c) {
             const int i0 = h * 64 + 2 * c;
-            const float p0 = ex2_approx(fmaf(sv[i0], p.scale_log2, -ms));
-            const float p1 = ex2_approx(fmaf(sv[i0 + 1], p.scale_log2, -ms));
-            rs8[c & 3] += p0 + p1;
+            float a, b;
+            f2_unpack(f2_fma(f2_pack(sv[i0], sv[i0 + 1]), scale2, neg_ms2), a, b);
+            const float p0 = ex2_approx(a), p1 = ex2_approx(b);
+            rs2[c & 1] = f2_add(rs2[c & 1], f2_pack(p0, p1));
             __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
             pk[c] = __uint_as_float(*reinterpret_cast<uint32_t*>(&h2));
           }
           tmem_st32(s_col + h * 32, pk);
         }
         tmem_wait_st();
-        l += (rs8[0] + rs8[1]) + (rs8[2] + rs8[3]);
+        float r0, r1, r2, r3;
+        f2_unpack(rs2[0], r0, r1);
+        f2_unpack(rs2[1], r2, r3);
+        l += (r0 + r1) + (r2 + r3);
         ++ts;
         tc_fence_before();
         __syncwarp();
