@@ -188,10 +188,34 @@ __device__ __forceinline__ void issue_group_tensor(const FwdParams& p, const CUt
 template <int D>
 __device__ __forceinline__ void issue_group(const FwdParams& p, const KvMaps& maps, const Work& w, int g, GroupSrc src,
                                             uint8_t* stage, uint64_t* full_bar, uint64_t policy) {
-  const uint32_t v_dst = smem_u32(stage) + g * p.box_rows * 128;
+  const int R = p.box_rows;
+  int valid = src.valid, page = src.page;
+  if (valid > 0 && (page < 0 || page >= p.num_blocks)) {
+    atomicCAS(p.err, 0, (int)kDevErrBadBlockId);
+    page = p.num_blocks;
+    valid = R;  // whole box out of range -> zeros
+  }
+  const uint32_t v_dst = smem_u32(stage) + g * R * 128;
   const uint32_t k_dst = v_dst + KvStage<D>::kTensorBytes;
-  issue_group_tensor<D>(p, &maps.k_box, &maps.k_row, w, src, k_dst, full_bar, policy);
-  issue_group_tensor<D>(p, &maps.v_box, &maps.v_row, w, src, v_dst, full_bar, policy);
+  // K and V of the same 64 columns back to back: both halves of a page row are requested
+  // together
+#pragma unroll
+  for (int ch = 0; ch < KvStage<D>::kPanels; ++ch) {
+    const uint32_t off = ch * KvStage<D>::kPanelBytes;
+    if (valid == R) {
+      tma_load_4d(k_dst + off, &maps.k_box, ch * 64, w.h, src.slot, page, full_bar, policy);
+      tma_load_4d(v_dst + off, &maps.v_box, ch * 64, w.h, src.slot, page, full_bar, policy);
+    } else if (valid == 0) {
+      tma_load_4d(k_dst + off, &maps.k_box, ch * 64, w.h, 0, p.num_blocks, full_bar, policy);
+      tma_load_4d(v_dst + off, &maps.v_box, ch * 64, w.h, 0, p.num_blocks, full_bar, policy);
+    } else {
+      for (int r = 0; r < R; ++r) {
+        const int sl = r < valid ? src.slot + r : p.block_size;  // slot index block_size is out of range -> zeros
+        tma_load_4d(k_dst + off + r * 128, &maps.k_row, ch * 64, w.h, sl, page, full_bar, policy);
+        tma_load_4d(v_dst + off + r * 128, &maps.v_row, ch * 64, w.h, sl, page, full_bar, policy);
+      }
+    }
+  }
 }
 
 // Gathers one whole tile (all groups) into `stage`; used where no prefetch is possible.
