@@ -39,36 +39,49 @@ __global__ void __launch_bounds__(128) combine_kernel(const __grid_constant__ Fw
   if (ns <= 1) return;
 
   const int64_t stride = (int64_t)p.total_q * p.hq;
-  float mx = -INFINITY;
-  for (int s = lane; s < ns; s += 32) mx = fmaxf(mx, p.split_lse[s * stride + pair]);
-  mx = warp_max(mx);
   __nv_bfloat16* dst = p.out + (int64_t)tok * p.o_s0 + (int64_t)qh * p.o_s1 + lane * EPL;
+  float acc[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) acc[e] = 0.f;
+  float mx = -INFINITY, wsum = 0.f;
+  // All split LSEs are loaded at once (lane s holds split s), then every partial row is
+  // requested independently of the others so their latencies overlap.
+  for (int s0 = 0; s0 < ns; s0 += 32) {
+    const int s = s0 + lane;
+    const float ls = s < ns ? p.split_lse[s * stride + pair] : -INFINITY;
+    const float cmx = warp_max(ls);
+    const float nmx = fmaxf(mx, cmx);
+    if (nmx == -INFINITY) continue;
+    const float scale_old = (mx == -INFINITY) ? 0.f : ex2_approx(mx - nmx);
+    wsum *= scale_old;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) acc[e] *= scale_old;
+    mx = nmx;
+    const float wl = (ls == -INFINITY) ? 0.f : ex2_approx(ls - mx);
+    wsum += warp_sum(wl);
+    const int cnt = ns - s0 < 32 ? ns - s0 : 32;
+#pragma unroll 4
+    for (int i = 0; i < cnt; ++i) {
+      const float wgt = __shfl_sync(0xffffffffu, wl, i);
+      const float* src = p.split_o + ((s0 + i) * stride + pair) * D + lane * EPL;
+      if constexpr (EPL == 4) {
+        const float4 v = *reinterpret_cast<const float4*>(src);
+        acc[0] += wgt * v.x;
+        acc[1] += wgt * v.y;
+        acc[2] += wgt * v.z;
+        acc[3] += wgt * v.w;
+      } else {
+        const float2 v = *reinterpret_cast<const float2*>(src);
+        acc[0] += wgt * v.x;
+        acc[1] += wgt * v.y;
+      }
+    }
+  }
   if (mx == -INFINITY) {
 #pragma unroll
     for (int e = 0; e < EPL; ++e) dst[e] = __float2bfloat16(0.f);
     if (lane == 0 && p.lse) p.lse[pair] = -INFINITY;
     return;
-  }
-  float acc[EPL];
-#pragma unroll
-  for (int e = 0; e < EPL; ++e) acc[e] = 0.f;
-  float wsum = 0.f;
-  for (int s = 0; s < ns; ++s) {
-    const float ls = p.split_lse[s * stride + pair];
-    const float wgt = (ls == -INFINITY) ? 0.f : ex2_approx(ls - mx);
-    wsum += wgt;
-    const float* src = p.split_o + (s * stride + pair) * D + lane * EPL;
-    if constexpr (EPL == 4) {
-      const float4 v = *reinterpret_cast<const float4*>(src);
-      acc[0] += wgt * v.x;
-      acc[1] += wgt * v.y;
-      acc[2] += wgt * v.z;
-      acc[3] += wgt * v.w;
-    } else {
-      const float2 v = *reinterpret_cast<const float2*>(src);
-      acc[0] += wgt * v.x;
-      acc[1] += wgt * v.y;
-    }
   }
   const float inv = 1.f / wsum;
 #pragma unroll

@@ -229,6 +229,10 @@ __device__ __forceinline__ void produce_tile(const FwdParams& p, const KvMaps& m
     issue_group<D>(p, maps, w, g, resolve_group(p, w, tile, g), stage, full_bar, policy);
 }
 
+#ifdef TFA_PROFILE
+__device__ void decode_stamp_hook(int i);
+#endif
+
 // Producer warp main loop shared by both kernels. Fetches work items dynamically,
 // publishes each into the two-slot item queue and streams their kv tiles. When a tile
 // has at most 32 groups (block_size >= 4), lane g owns group g and the block-table
@@ -266,6 +270,9 @@ __device__ __forceinline__ void producer_loop(const FwdParams& p, const KvMaps& 
       mbar_arrive(&item_full[slot]);
     }
     if (idx >= p.num_items) return;
+#ifdef TFA_PROFILE
+    if (lane == 0 && k == 0 && blockIdx.x == 0 && p.rows_per_tile == 16) decode_stamp_hook(2);
+#endif
     if (w.tile_end == w.tile_begin) claim();
     if (lane_per_group) {
       GroupSrc cur{}, nxt{};
@@ -281,6 +288,9 @@ __device__ __forceinline__ void producer_loop(const FwdParams& p, const KvMaps& 
         if (lane == 0) mbar_arrive_expect_tx(&full[st], KvStage<D>::kBytes);
         __syncwarp();
         if (lane < groups) issue_group<D>(p, maps, w, lane, cur, stages + st * KvStage<D>::kBytes, &full[st], policy);
+#ifdef TFA_PROFILE
+        if (lane == 0 && c == 0 && blockIdx.x == 0 && p.rows_per_tile == 16) decode_stamp_hook(3);
+#endif
         cur = nxt;
       }
     } else {
@@ -371,6 +381,30 @@ __device__ __forceinline__ float warp_max(float v) {
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   return v;
 }
+// Reduces 16 per-lane columns over the 32 lanes of a warp with a transposing butterfly
+// (8 + 4 + 2 + 1 + 1 shuffles instead of 16 x 5). On return, lane L holds the total of
+// column col16_of_lane(L); v is clobbered.
+template <bool kMax>
+__device__ __forceinline__ float col16_reduce(float (&v)[16], int lane) {
+  auto op = [](float a, float b) { return kMax ? fmaxf(a, b) : a + b; };
+#pragma unroll
+  for (int step = 0; step < 4; ++step) {
+    const int m = 16 >> step;    // lane mask of this step
+    const int half = 8 >> step;  // columns kept after it
+    const bool hi = (lane & m) != 0;
+#pragma unroll
+    for (int i = 0; i < half; ++i) {
+      const float send = hi ? v[i] : v[i + half];
+      const float keep = hi ? v[i + half] : v[i];
+      v[i] = op(keep, __shfl_xor_sync(0xffffffffu, send, m));
+    }
+  }
+  return op(v[0], __shfl_xor_sync(0xffffffffu, v[0], 1));
+}
+__device__ __forceinline__ int col16_of_lane(int lane) {
+  return ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

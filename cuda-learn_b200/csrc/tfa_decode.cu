@@ -23,6 +23,16 @@ namespace {
 
 constexpr int kNP = 16;  // packed q rows (MMA N)
 
+#ifdef TFA_PROFILE
+__device__ unsigned long long g_decode_stamp[32];
+#define STAMP(i) do { if (blockIdx.x == 0) g_decode_stamp[i] = global_timer_ns(); } while (0)
+}  // namespace
+__device__ void decode_stamp_hook(int i) { g_decode_stamp[i] = global_timer_ns(); }
+namespace {
+#else
+#define STAMP(i) do {} while (0)
+#endif
+
 template <int D>
 struct DecodeCfg {
   static constexpr int kPanels = D / 64;
@@ -52,12 +62,13 @@ __global__ void __launch_bounds__(192, 1)
   __shared__ int item_slot[2];
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_flag;
-  __shared__ float red_max[2][4][kNP];
-  __shared__ float red_sum[2][4][kNP];
+  __shared__ __align__(16) float red_max[2][4][kNP];
+  __shared__ __align__(16) float red_sum[2][4][kNP];
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
+  if (tid == 0) STAMP(0);
 
   if (tid == 0) {
     for (int i = 0; i < Cfg::kStages; ++i) {
@@ -88,6 +99,7 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tmem = tmem_base_sh;
   if (tid == 0) allow_dependent_launch();
+  if (tid == 0) STAMP(1);
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -108,6 +120,7 @@ __global__ void __launch_bounds__(192, 1)
       const Work w = get_work(p, idx);
       const int n = w.tile_end - w.tile_begin;
       if (!mbar_wait(&q_full[slot], (k >> 1) & 1, &abort_flag, p.err, kDevErrTimeoutMma)) break;
+      if (lane == 0 && k == 0) STAMP(4);
       if (lane == 0 && n > 0) {
         auto issue_qk = [&](int cc) -> bool {
           const int st = cc % Cfg::kStages;
@@ -124,6 +137,7 @@ __global__ void __launch_bounds__(192, 1)
                          idesc_qk, kk > 0 ? 1u : 0u);
           }
           umma_commit(&s_full[cc & 1]);
+          if (cc == 0) STAMP(5);
           return true;
         };
         ok = issue_qk(c);
@@ -175,6 +189,7 @@ __global__ void __launch_bounds__(192, 1)
     for (int k = 0;; ++k) {
       const int slot = k & 1;
       if (!mbar_wait(&item_full[slot], (k >> 1) & 1, &abort_flag, p.err, kDevErrTimeoutSoftmax)) break;
+      if (warp == 2 && lane == 0 && k == 0) STAMP(6);
       const int idx = item_slot[slot];
       if (idx >= p.num_items) break;
       const Work w = get_work(p, idx);
@@ -197,17 +212,24 @@ __global__ void __launch_bounds__(192, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&q_full[slot]);
+        if (warp == 2 && lane == 0 && k == 0) STAMP(7);
       }
 
+      // Per-row constants, computed by lane r for row r and broadcast: visible kv range,
+      // and where the row's output goes.
+      int lo_l = 1, hi_l = 0, tok_l = 0, qh_l = 0;
+      if (lane < w.nrows) {
+        const int R = w.row0 + lane;
+        tok_l = R / p.group;
+        qh_l = w.h * p.group + (R - tok_l * p.group);
+        visible_range(p, tok_l, w.q_len, w.kv_len, lo_l, hi_l);
+        tok_l += w.q0;
+      }
       int lo[kNP], hi[kNP];
 #pragma unroll
       for (int r = 0; r < kNP; ++r) {
-        if (r < w.nrows) {
-          visible_range(p, (w.row0 + r) / p.group, w.q_len, w.kv_len, lo[r], hi[r]);
-        } else {
-          lo[r] = 1;
-          hi[r] = 0;
-        }
+        lo[r] = __shfl_sync(0xffffffffu, lo_l, r);
+        hi[r] = __shfl_sync(0xffffffffu, hi_l, r);
       }
       float m[kNP], l[kNP], o[kNP], a_prev[kNP];
 #pragma unroll
@@ -225,6 +247,7 @@ __global__ void __launch_bounds__(192, 1)
           break;
         }
         tc_fence_after();
+        if (warp == 2 && lane == 0 && cj == 0) STAMP(8);
         float s[kNP];
         tmem_ld16(lane_base + (cj & 1) * kNP, s);
         tmem_wait_ld();
@@ -235,19 +258,33 @@ __global__ void __launch_bounds__(192, 1)
         const int pos = (w.tile_begin + j) * kBN + tl;
         float a[kNP];
 #pragma unroll
-        for (int r = 0; r < kNP; ++r) {
-          s[r] = (pos >= lo[r] && pos <= hi[r]) ? s[r] * p.scale_log2 : -INFINITY;
-          const float wm = warp_max(s[r]);
-          if (lane == 0) red_max[cj & 1][sw][r] = wm;
+        for (int r = 0; r < kNP; ++r) s[r] = (pos >= lo[r] && pos <= hi[r]) ? s[r] * p.scale_log2 : -INFINITY;
+        {
+          float t[kNP];
+#pragma unroll
+          for (int r = 0; r < kNP; ++r) t[r] = s[r];
+          const float wm = col16_reduce<true>(t, lane);
+          if ((lane & 1) == 0) red_max[cj & 1][sw][col16_of_lane(lane)] = wm;
         }
         if (!sm_sync()) {
           ok = false;
           break;
         }
+        float cmax[kNP];
+#pragma unroll
+        for (int q4 = 0; q4 < kNP / 4; ++q4) {
+          float4 a0 = *reinterpret_cast<const float4*>(&red_max[cj & 1][0][q4 * 4]);
+          float4 a1 = *reinterpret_cast<const float4*>(&red_max[cj & 1][1][q4 * 4]);
+          float4 a2 = *reinterpret_cast<const float4*>(&red_max[cj & 1][2][q4 * 4]);
+          float4 a3 = *reinterpret_cast<const float4*>(&red_max[cj & 1][3][q4 * 4]);
+          cmax[q4 * 4 + 0] = fmaxf(fmaxf(a0.x, a1.x), fmaxf(a2.x, a3.x));
+          cmax[q4 * 4 + 1] = fmaxf(fmaxf(a0.y, a1.y), fmaxf(a2.y, a3.y));
+          cmax[q4 * 4 + 2] = fmaxf(fmaxf(a0.z, a1.z), fmaxf(a2.z, a3.z));
+          cmax[q4 * 4 + 3] = fmaxf(fmaxf(a0.w, a1.w), fmaxf(a2.w, a3.w));
+        }
 #pragma unroll
         for (int r = 0; r < kNP; ++r) {
-          const float tmax = fmaxf(fmaxf(red_max[cj & 1][0][r], red_max[cj & 1][1][r]),
-                                   fmaxf(red_max[cj & 1][2][r], red_max[cj & 1][3][r]));
+          const float tmax = cmax[r];
           const float mn = fmaxf(m[r], tmax);
           a[r] = (m[r] == -INFINITY) ? 1.f : ex2_approx(m[r] - mn);
           const float ms = (mn == -INFINITY) ? 0.f : mn;
@@ -283,6 +320,7 @@ __global__ void __launch_bounds__(192, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[cj & 1]);
+        if (warp == 2 && lane == 0 && cj == 0) STAMP(9);
       }
       if (ok && n > 0) {
         const int cl = c + n - 1;
@@ -301,37 +339,59 @@ __global__ void __launch_bounds__(192, 1)
         }
       }
       if (!ok) break;
+      if (warp == 2 && lane == 0 && k == 0) STAMP(10);
       c += n;
 
       // column sums of the per-token partial denominators
+      {
+        float t[kNP];
 #pragma unroll
-      for (int r = 0; r < kNP; ++r) {
-        const float ws = warp_sum(l[r]);
-        if (lane == 0) red_sum[k & 1][sw][r] = ws;
+        for (int r = 0; r < kNP; ++r) t[r] = l[r];
+        const float ws = col16_reduce<false>(t, lane);
+        if ((lane & 1) == 0) red_sum[k & 1][sw][col16_of_lane(lane)] = ws;
       }
+      if (warp == 2 && lane == 0 && k == 0) STAMP(15);
       if (!sm_sync()) break;
+      if (warp == 2 && lane == 0 && k == 0) STAMP(16);
       const bool direct = (w.nsplits == 1);
+      // lane r: normaliser, LSE and destination of row r
+      float inv_l = 0.f;
+      int64_t dst_l = 0;
+      if (lane < w.nrows) {
+        const float lsum = red_sum[k & 1][0][lane] + red_sum[k & 1][1][lane] + red_sum[k & 1][2][lane] +
+                           red_sum[k & 1][3][lane];
+        inv_l = lsum > 0.f ? __frcp_rn(lsum) : 0.f;
+        dst_l = direct ? (int64_t)tok_l * p.o_s0 + (int64_t)qh_l * p.o_s1
+                       : (((int64_t)w.split * p.total_q + tok_l) * p.hq + qh_l);
+        if (sw == 0) {
+          // m[] is replicated in every thread; this lane needs m[lane]
+          float ml = -INFINITY;
+#pragma unroll
+          for (int r = 0; r < kNP; ++r) ml = (r == lane) ? m[r] : ml;
+          const float lse2 = lsum > 0.f ? ml + lg2_approx(lsum) : -INFINITY;
+          if (direct) {
+            if (p.lse) p.lse[(int64_t)tok_l * p.hq + qh_l] = lse2 * kLn2;
+          } else {
+            p.split_lse[dst_l] = lse2;
+          }
+        }
+      }
 #pragma unroll
       for (int r = 0; r < kNP; ++r) {
         if (r >= w.nrows) break;
-        const float lsum = red_sum[k & 1][0][r] + red_sum[k & 1][1][r] + red_sum[k & 1][2][r] + red_sum[k & 1][3][r];
-        const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
-        const int R = w.row0 + r;
-        const int tok = w.q0 + R / p.group;
-        const int qh = w.h * p.group + R % p.group;
-        const float lse2 = lsum > 0.f ? m[r] + lg2_approx(lsum) : -INFINITY;
-        if (direct) {
-          if (tl < D) p.out[(int64_t)tok * p.o_s0 + (int64_t)qh * p.o_s1 + tl] = __float2bfloat16(o[r] * inv);
-          if (tq == 0 && p.lse) p.lse[(int64_t)tok * p.hq + qh] = lse2 * kLn2;
-        } else {
-          const int64_t row = ((int64_t)w.split * p.total_q + tok) * p.hq + qh;
-          if (tl < D) p.split_o[row * D + tl] = o[r] * inv;
-          if (tq == 0) p.split_lse[row] = lse2;
+        const float inv = __shfl_sync(0xffffffffu, inv_l, r);
+        const int64_t dst = __shfl_sync(0xffffffffu, dst_l, r);
+        if (tl < D) {
+          if (direct) p.out[dst + tl] = __float2bfloat16(o[r] * inv);
+          else p.split_o[dst * D + tl] = o[r] * inv;
         }
+        if (warp == 2 && lane == 0 && k == 0 && r == 0) STAMP(17);
       }
       __syncwarp();
+      if (warp == 2 && lane == 0 && k == 0) STAMP(11);
       if (lane == 0) mbar_arrive(&item_empty[slot]);
     }
+    if (warp == 2 && lane == 0) STAMP(12);
   }
 
   if (abort_flag && warp == 0) {
@@ -342,11 +402,13 @@ __global__ void __launch_bounds__(192, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if (tid == 0) STAMP(13);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, Cfg::kTmemCols);
   }
   if (tid == 0) scheduler_finish(p);
+  if (tid == 0) STAMP(14);
 }
 
 }  // namespace
@@ -371,6 +433,12 @@ cudaError_t launch_decode(const FwdParams& p, const KvMaps& maps, int grid, cuda
   decode_kernel<D><<<grid, 192, DecodeCfg<D>::kDynBytes, s>>>(p, maps);
   return cudaGetLastError();
 }
+
+#ifdef TFA_PROFILE
+extern "C" __attribute__((visibility("default"))) int tfa_decode_stamps_read(unsigned long long* host) {
+  return (int)cudaMemcpyFromSymbol(host, g_decode_stamp, sizeof(g_decode_stamp));
+}
+#endif
 
 template int decode_smem_bytes<64>();
 template int decode_smem_bytes<128>();
