@@ -117,6 +117,19 @@ __device__ __forceinline__ Work get_work(const FwdParams& p, int idx) {
   return w;
 }
 
+// Called once per CTA by the producer's lane 0 after its final (out-of-range) claim: no
+// claim can follow it from this CTA, so when every CTA has passed here the last one
+// resets the scheduler counters for the next launch on the same stream. Done by the
+// producer as soon as it stops claiming, off the consumers' critical path.
+__device__ __forceinline__ void scheduler_finish(const FwdParams& p) {
+  __threadfence();
+  if (atomicAdd(&p.sched[1], 1) == (int)gridDim.x - 1) {
+    atomicExch(&p.sched[0], 0);
+    atomicExch(&p.sched[1], 0);
+    __threadfence();
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Paged K/V producer: one warp gathers the 128-token tile of kv head h of sequence b
 // into a pipeline stage laid out as [V panels][K panels], each panel 128 rows x 128 B
@@ -269,7 +282,10 @@ __device__ __forceinline__ void producer_loop(const FwdParams& p, const KvMaps& 
       item_slot[slot] = idx;
       mbar_arrive(&item_full[slot]);
     }
-    if (idx >= p.num_items) return;
+    if (idx >= p.num_items) {
+      if (lane == 0) scheduler_finish(p);
+      return;
+    }
 #ifdef TFA_PROFILE
     if (lane == 0 && k == 0 && blockIdx.x == 0 && p.rows_per_tile == 16) decode_stamp_hook(2);
 #endif
@@ -335,7 +351,10 @@ __device__ __forceinline__ void producer_loop_kv_slots(const FwdParams& p, const
       item_slot[slot] = idx;
       mbar_arrive(&item_full[slot]);
     }
-    if (idx >= p.num_items) return;
+    if (idx >= p.num_items) {
+      if (lane == 0) scheduler_finish(p);
+      return;
+    }
     if (w.tile_end == w.tile_begin) claim();
     for (int t = w.tile_begin; t < w.tile_end; ++t) {
       if (t + 1 == w.tile_end) claim();
@@ -355,17 +374,6 @@ __device__ __forceinline__ void producer_loop_kv_slots(const FwdParams& p, const
         }
       }
     }
-  }
-}
-
-// Grid-wide epilogue: the last CTA to finish resets the scheduler counters so the
-// workspace is ready for the next launch on the same stream.
-__device__ __forceinline__ void scheduler_finish(const FwdParams& p) {
-  __threadfence();
-  if (atomicAdd(&p.sched[1], 1) == (int)gridDim.x - 1) {
-    atomicExch(&p.sched[0], 0);
-    atomicExch(&p.sched[1], 0);
-    __threadfence();
   }
 }
 

@@ -407,7 +407,6 @@ __global__ void __launch_bounds__(192, 1)
     tc_fence_after();
     tmem_dealloc(tmem, Cfg::kTmemCols);
   }
-  if (tid == 0) scheduler_finish(p);
   if (tid == 0) STAMP(14);
 }
 

@@ -415,7 +415,6 @@ __global__ void __launch_bounds__(320, 1)
     tc_fence_after();
     tmem_dealloc(tmem, Cfg::kTmemCols);
   }
-  if (tid == 0) scheduler_finish(p);
 }
 
 }  // namespace

@@ -140,8 +140,9 @@ TFA_API int tfa_fwd_timed(const tfa_fwd_params* p, void* workspace, size_t works
 TFA_API int tfa_fwd_static_workspace(const tfa_fwd_params* p, void* stream);
 
 /* Synchronises `stream`, copies the device error word of `workspace` into *err (0 = none)
- * and clears it. A non-zero word means a kernel hit an internal time limit or found a
- * block id outside [0, num_blocks) (those rows were read as zeros). */
+ * and clears it. A non-zero word means a kernel hit an internal time limit (codes
+ * 101-103; the workspace must then be zero-filled again before reuse) or found a block id
+ * outside [0, num_blocks) (code 110; those rows were read as zeros). */
 TFA_API int tfa_read_device_error(void* workspace, void* stream, int* err);
 
 /* Number of SMs of `device` (cached). */
