@@ -122,10 +122,8 @@ __global__ void __launch_bounds__(192, 1)
       if (!mbar_wait(&q_full[slot], (k >> 1) & 1, &abort_flag, p.err, kDevErrTimeoutMma)) break;
       if (lane == 0 && k == 0) STAMP(4);
       if (lane == 0 && n > 0) {
-        auto issue_qk = [&](int cc) -> bool {
+        auto issue_qk = [&](int cc) {
           const int st = cc % Cfg::kStages;
-          if (!mbar_wait(&full[st], (cc / Cfg::kStages) & 1, &abort_flag, p.err, kDevErrTimeoutMma)) return false;
-          if (!mbar_wait(&s_free[cc & 1], ((cc >> 1) & 1) ^ 1, &abort_flag, p.err, kDevErrTimeoutMma)) return false;
           tc_fence_after();
           const uint32_t k_addr = smem_u32(stages + st * Cfg::kStageBytes) + KvStage<D>::kTensorBytes;
           const uint32_t d_tmem = tmem + (cc & 1) * kNP;
@@ -137,18 +135,8 @@ __global__ void __launch_bounds__(192, 1)
                          idesc_qk, kk > 0 ? 1u : 0u);
           }
           umma_commit(&s_full[cc & 1]);
-          if (cc == 0) STAMP(5);
-          return true;
         };
-        ok = issue_qk(c);
-        for (int j = 0; ok && j < n; ++j) {
-          const int cj = c + j;
-          if (j + 1 < n && !(ok = issue_qk(cj + 1))) break;
-          if (!mbar_wait(&p_full[cj & 1], (cj >> 1) & 1, &abort_flag, p.err, kDevErrTimeoutMma) ||
-              !mbar_wait(&o_free[cj & 1], ((cj >> 1) & 1) ^ 1, &abort_flag, p.err, kDevErrTimeoutMma)) {
-            ok = false;
-            break;
-          }
+        auto issue_pv = [&](int cj) {
           tc_fence_after();
           const int st = cj % Cfg::kStages;
           const uint32_t v_addr = smem_u32(stages + st * Cfg::kStageBytes);
@@ -161,8 +149,54 @@ __global__ void __launch_bounds__(192, 1)
             umma_bf16_ss(d_tmem, make_sdesc_sw128(v_addr + voff, KvStage<D>::kPanelBytes, 1024),
                          make_sdesc_sw128(pb + poff, 16, 1024), idesc_pv, kk > 0 ? 1u : 0u);
           }
-          umma_commit(&empty[st]);
+          umma_commit(&empty[st]);  // frees the K/V stage once this P.V (and all before it) completes
           umma_commit(&o_full[cj & 1]);
+        };
+        // QK of tile jq and P.V of tile jp are issued as soon as each one's inputs are
+        // ready, in whichever order that happens: a P.V (which frees its stage) never
+        // waits behind the next tile's K/V arrival, so all stages stay in flight while
+        // the kernel is bound by HBM. QK runs at most two tiles ahead (two S buffers).
+        int jq = 0, jp = 0;
+        uint32_t idle = 0;
+        uint64_t t0 = 0;
+        while (jp < n) {
+          bool progress = false;
+          if (jq < n && jq < jp + 2) {
+            const int cq = c + jq;
+            if (mbar_test(&full[cq % Cfg::kStages], (cq / Cfg::kStages) & 1) &&
+                mbar_test(&s_free[cq & 1], ((cq >> 1) & 1) ^ 1)) {
+              issue_qk(cq);
+              ++jq;
+              progress = true;
+            }
+          }
+          if (jp < jq) {
+            const int cp = c + jp;
+            if (mbar_test(&p_full[cp & 1], (cp >> 1) & 1) && mbar_test(&o_free[cp & 1], ((cp >> 1) & 1) ^ 1)) {
+              issue_pv(cp);
+              ++jp;
+              progress = true;
+            }
+          }
+          if (progress) {
+            idle = 0;
+            continue;
+          }
+          // bounded: same wall-clock limit and abort protocol as mbar_wait
+          if (idle++ == 0) {
+            t0 = global_timer_ns();
+          } else if ((idle & 63u) == 0) {
+            if (abort_flag) {
+              ok = false;
+              break;
+            }
+            if (global_timer_ns() - t0 > kWaitLimitNs) {
+              abort_flag = 1;
+              atomicCAS(p.err, 0, kDevErrTimeoutMma);
+              ok = false;
+              break;
+            }
+          }
         }
       }
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
