@@ -210,15 +210,21 @@ __device__ __forceinline__ void issue_group(const FwdParams& p, const KvMaps& ma
   }
   const uint32_t v_dst = smem_u32(stage) + g * R * 128;
   const uint32_t k_dst = v_dst + KvStage<D>::kTensorBytes;
-  // K and V of the same 64 columns back to back: both halves of a page row are requested
-  // together
+  if (valid == R) {
+    // Full group: all K boxes (its 64-column panels are adjacent in memory), then all V
+    // boxes. With one lane per group the warp issues each box for every group in turn.
+#pragma unroll
+    for (int ch = 0; ch < KvStage<D>::kPanels; ++ch)
+      tma_load_4d(k_dst + ch * KvStage<D>::kPanelBytes, &maps.k_box, ch * 64, w.h, src.slot, page, full_bar, policy);
+#pragma unroll
+    for (int ch = 0; ch < KvStage<D>::kPanels; ++ch)
+      tma_load_4d(v_dst + ch * KvStage<D>::kPanelBytes, &maps.v_box, ch * 64, w.h, src.slot, page, full_bar, policy);
+    return;
+  }
 #pragma unroll
   for (int ch = 0; ch < KvStage<D>::kPanels; ++ch) {
     const uint32_t off = ch * KvStage<D>::kPanelBytes;
-    if (valid == R) {
-      tma_load_4d(k_dst + off, &maps.k_box, ch * 64, w.h, src.slot, page, full_bar, policy);
-      tma_load_4d(v_dst + off, &maps.v_box, ch * 64, w.h, src.slot, page, full_bar, policy);
-    } else if (valid == 0) {
+    if (valid == 0) {
       tma_load_4d(k_dst + off, &maps.k_box, ch * 64, w.h, 0, p.num_blocks, full_bar, policy);
       tma_load_4d(v_dst + off, &maps.v_box, ch * 64, w.h, 0, p.num_blocks, full_bar, policy);
     } else {
