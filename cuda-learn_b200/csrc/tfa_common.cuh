@@ -237,6 +237,22 @@ __device__ __forceinline__ void issue_group(const FwdParams& p, const KvMaps& ma
   }
 }
 
+// Boxes of one group of one tensor (tensor 1 = K, 0 = V) into its half of `stage`.
+template <int D>
+__device__ __forceinline__ void issue_group_one(const FwdParams& p, const KvMaps& maps, const Work& w, int g,
+                                                GroupSrc src, int tensor, uint8_t* stage, uint64_t* full_bar,
+                                                uint64_t policy) {
+  const uint32_t dst = smem_u32(stage) + g * p.box_rows * 128 + tensor * KvStage<D>::kTensorBytes;
+  const CUtensorMap* box = tensor ? &maps.k_box : &maps.v_box;
+  if (src.valid == p.box_rows && src.page >= 0 && src.page < p.num_blocks) {
+#pragma unroll
+    for (int ch = 0; ch < KvStage<D>::kPanels; ++ch)
+      tma_load_4d(dst + ch * KvStage<D>::kPanelBytes, box, ch * 64, w.h, src.slot, src.page, full_bar, policy);
+    return;
+  }
+  issue_group_tensor<D>(p, box, tensor ? &maps.k_row : &maps.v_row, w, src, dst, full_bar, policy);
+}
+
 // Gathers one whole tile (all groups) into `stage`; used where no prefetch is possible.
 template <int D>
 __device__ __forceinline__ void produce_tile(const FwdParams& p, const KvMaps& maps, const Work& w, int tile,
@@ -307,9 +323,9 @@ __device__ __forceinline__ void producer_loop(const FwdParams& p, const KvMaps& 
         }
         const int st = c % STAGES;
         if (!mbar_wait(&empty[st], ((c / STAGES) & 1) ^ 1, abort_flag, p.err, kDevErrTimeoutProducer)) return;
-        if (lane == 0) mbar_arrive_expect_tx(&full[st], KvStage<D>::kBytes);
+        if (lane == 0) mbar_arrive_expect_tx(&full[st], KvStage<D>::kTensorBytes);
         __syncwarp();
-        if (lane < groups) issue_group<D>(p, maps, w, lane, cur, stages + st * KvStage<D>::kBytes, &full[st], policy);
+        if (lane < groups) issue_group_one<D>(p, maps, w, lane, cur, 1, stages + st * KvStage<D>::kBytes, &full[st], policy);
 #ifdef TFA_PROFILE
         if (lane == 0 && c == 0 && blockIdx.x == 0 && p.rows_per_tile == 16) decode_stamp_hook(3);
 #endif
@@ -320,9 +336,54 @@ __device__ __forceinline__ void producer_loop(const FwdParams& p, const KvMaps& 
         if (t + 1 == w.tile_end) claim();
         const int st = c % STAGES;
         if (!mbar_wait(&empty[st], ((c / STAGES) & 1) ^ 1, abort_flag, p.err, kDevErrTimeoutProducer)) return;
-        produce_tile<D>(p, maps, w, t, stages + st * KvStage<D>::kBytes, &full[st], lane, policy);
+        if (lane == 0) mbar_arrive_expect_tx(&full[st], KvStage<D>::kTensorBytes);
+        __syncwarp();
+        for (int g = lane; g < groups; g += 32)
+          issue_group_one<D>(p, maps, w, g, resolve_group(p, w, t, g), 1, stages + st * KvStage<D>::kBytes, &full[st],
+                             policy);
       }
     }
+  }
+}
+
+// Second producer warp of the decode kernel: follows the item queue like a consumer and
+// requests the V half of every stage (the first producer requests the K half), so the two
+// warps' barrier waits and loop overhead overlap each other's TMA issue. Each stage's
+// full barrier therefore expects two arrivals.
+template <int D, int STAGES>
+__device__ __forceinline__ void producer_follow_v(const FwdParams& p, const KvMaps& maps, uint8_t* stages,
+                                                  uint64_t* full, uint64_t* empty, uint64_t* item_full,
+                                                  uint64_t* item_empty, const int* item_slot,
+                                                  volatile int* abort_flag, int lane) {
+  const uint64_t policy = l2_policy_evict_first();
+  const int groups = kBN / p.box_rows;
+  const bool lane_per_group = groups <= 32;
+  int c = 0;
+  for (int k = 0;; ++k) {
+    const int slot = k & 1;
+    if (!mbar_wait(&item_full[slot], (k >> 1) & 1, abort_flag, p.err, kDevErrTimeoutProducer)) return;
+    const int idx = item_slot[slot];
+    if (idx >= p.num_items) return;
+    const Work w = get_work(p, idx);
+    GroupSrc cur{}, nxt{};
+    if (lane_per_group && lane < groups && w.tile_begin < w.tile_end) cur = resolve_group(p, w, w.tile_begin, lane);
+    for (int t = w.tile_begin; t < w.tile_end; ++t, ++c) {
+      if (lane_per_group && lane < groups && t + 1 < w.tile_end) nxt = resolve_group(p, w, t + 1, lane);
+      const int st = c % STAGES;
+      if (!mbar_wait(&empty[st], ((c / STAGES) & 1) ^ 1, abort_flag, p.err, kDevErrTimeoutProducer)) return;
+      if (lane == 0) mbar_arrive_expect_tx(&full[st], KvStage<D>::kTensorBytes);
+      __syncwarp();
+      if (lane_per_group) {
+        if (lane < groups) issue_group_one<D>(p, maps, w, lane, cur, 0, stages + st * KvStage<D>::kBytes, &full[st], policy);
+      } else {
+        for (int g = lane; g < groups; g += 32)
+          issue_group_one<D>(p, maps, w, g, resolve_group(p, w, t, g), 0, stages + st * KvStage<D>::kBytes, &full[st],
+                             policy);
+      }
+      cur = nxt;
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&item_empty[slot]);
   }
 }
 

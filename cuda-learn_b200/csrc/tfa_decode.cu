@@ -11,8 +11,8 @@
 // write P^T back to shared memory for the second MMA. The un-normalised output of each
 // tile is folded into registers (thread = head-dim lane) with the running rescale.
 //
-// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = MMA issuer + TMEM owner,
-// warps 2-5 = softmax / epilogue.
+// Warp roles (224 threads): warp 0 = TMA producer of K (and the item scheduler), warp 6 =
+// TMA producer of V, warp 1 = MMA issuer + TMEM owner, warps 2-5 = softmax / epilogue.
 #include <cmath>
 
 #include "tfa_common.cuh"
@@ -47,7 +47,7 @@ struct DecodeCfg {
 };
 
 template <int D>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(224, 1)
     decode_kernel(const __grid_constant__ FwdParams p, const __grid_constant__ KvMaps maps) {
   using Cfg = DecodeCfg<D>;
   extern __shared__ uint8_t dyn_smem[];
@@ -72,7 +72,7 @@ __global__ void __launch_bounds__(192, 1)
 
   if (tid == 0) {
     for (int i = 0; i < Cfg::kStages; ++i) {
-      mbar_init(&full[i], 1);
+      mbar_init(&full[i], 2);  // K and V producers
       mbar_init(&empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -82,7 +82,7 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&o_full[i], 1);
       mbar_init(&o_free[i], 4);
       mbar_init(&item_full[i], 1);
-      mbar_init(&item_empty[i], 5);
+      mbar_init(&item_empty[i], 6);
       mbar_init(&q_full[i], 4);
     }
     mbar_init(&red_bar, 4);
@@ -105,6 +105,8 @@ __global__ void __launch_bounds__(192, 1)
     // ------------------------------------------------------------ producer
     producer_loop<D, Cfg::kStages>(p, maps, stages, full, empty, item_full, item_empty, item_slot, &abort_flag,
                                    lane);
+  } else if (warp == 6) {
+    producer_follow_v<D, Cfg::kStages>(p, maps, stages, full, empty, item_full, item_empty, item_slot, &abort_flag, lane);
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     const uint32_t idesc_qk = make_idesc_bf16_f32(128, kNP, false, false);
@@ -428,7 +430,7 @@ __global__ void __launch_bounds__(192, 1)
     if (warp == 2 && lane == 0) STAMP(12);
   }
 
-  if (abort_flag && warp == 0) {
+  if (abort_flag && (warp == 0 || warp == 6)) {
     // Let TMA copies that may still be in flight land before the CTA's shared memory
     // is released (bounded: 100 us).
     const uint64_t t0 = global_timer_ns();
@@ -463,7 +465,7 @@ cudaError_t launch_decode(const FwdParams& p, const KvMaps& maps, int grid, cuda
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
-  decode_kernel<D><<<grid, 192, DecodeCfg<D>::kDynBytes, s>>>(p, maps);
+  decode_kernel<D><<<grid, 224, DecodeCfg<D>::kDynBytes, s>>>(p, maps);
   return cudaGetLastError();
 }
 
