@@ -271,13 +271,19 @@ int fwd_impl(const tfa_fwd_params* a, void* workspace, size_t workspace_bytes, v
   fill_params(a, pl, workspace, &p);
   KvMaps maps;
   if ((rc = encode_maps(a, p.box_rows, &maps)) != TFA_OK) return rc;
+  CUtensorMap q_map;  // decode kernel only: (64 columns, group heads, 16 / group tokens) boxes of q
+  std::memset(&q_map, 0, sizeof(q_map));
+  if (pl.kernel == 0 &&
+      encode_q_map(&q_map, a->q, a->total_q, a->num_q_heads, a->head_dim, a->q_stride[0], a->q_stride[1],
+                   (uint32_t)p.group, (uint32_t)(16 / p.group)) != 0)
+    return TFA_ERR_TENSOR_MAP;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   cudaError_t e;
   if (ev_begin && cudaEventRecord(reinterpret_cast<cudaEvent_t>(ev_begin), s) != cudaSuccess) return TFA_ERR_CUDA;
   if (a->head_dim == 64)
-    e = pl.kernel == 0 ? launch_decode<64>(p, maps, pl.grid, s) : launch_prefill<64>(p, maps, pl.grid, s);
+    e = pl.kernel == 0 ? launch_decode<64>(p, maps, q_map, pl.grid, s) : launch_prefill<64>(p, maps, pl.grid, s);
   else
-    e = pl.kernel == 0 ? launch_decode<128>(p, maps, pl.grid, s) : launch_prefill<128>(p, maps, pl.grid, s);
+    e = pl.kernel == 0 ? launch_decode<128>(p, maps, q_map, pl.grid, s) : launch_prefill<128>(p, maps, pl.grid, s);
   if (e != cudaSuccess) {
     if (std::getenv("TFA_DEBUG")) std::fprintf(stderr, "tfa_fwd: launch failed: %s\n", cudaGetErrorString(e));
     return TFA_ERR_CUDA;

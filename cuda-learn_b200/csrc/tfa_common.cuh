@@ -268,8 +268,9 @@ __device__ __forceinline__ void produce_tile(const FwdParams& p, const KvMaps& m
 __device__ void decode_stamp_hook(int i);
 #endif
 
-// Producer warp main loop shared by both kernels. Fetches work items dynamically,
-// publishes each into the two-slot item queue and streams their kv tiles. When a tile
+// Producer warp main loop of the decode kernel. Fetches work items dynamically,
+// publishes each (index, descriptor, and its Q rows loaded by TMA) into the two-slot item
+// queue and streams their kv tiles, so the consumers start an item without global loads. When a tile
 // has at most 32 groups (block_size >= 4), lane g owns group g and the block-table
 // entries of tile t+1 are requested before the wait for tile t's free stage, so the
 // table latency hides behind the pipeline; the next item is claimed while the last tile
@@ -278,11 +279,14 @@ __device__ void decode_stamp_hook(int i);
 template <int D, int STAGES>
 __device__ __forceinline__ void producer_loop(const FwdParams& p, const KvMaps& maps, uint8_t* stages,
                                               uint64_t* full, uint64_t* empty, uint64_t* item_full,
-                                              uint64_t* item_empty, int* item_slot, volatile int* abort_flag,
-                                              int lane) {
+                                              uint64_t* item_empty, int* item_slot, Work* item_work,
+                                              const CUtensorMap* q_map, uint8_t* q_bufs, int q_buf_bytes,
+                                              uint64_t* q_full, volatile int* abort_flag, int lane) {
   const uint64_t policy = l2_policy_evict_first();
   const int groups = kBN / p.box_rows;
   const bool lane_per_group = groups <= 32;
+  const int q_tokens = 16 / p.group;  // tokens per Q box (G heads each)
+  const uint32_t q_tx = (uint32_t)(KvStage<D>::kPanels * p.group * q_tokens * 128);
   int c = 0;
   int claimed = (lane == 0) ? (int)blockIdx.x : 0;  // next item index (lane 0)
   auto claim = [&]() {
@@ -302,6 +306,17 @@ __device__ __forceinline__ void producer_loop(const FwdParams& p, const KvMaps& 
     }
     if (lane == 0) {
       item_slot[slot] = idx;
+      if (idx < p.num_items) {
+        // The item's descriptor and Q rows (all heads of the group, its tokens, packed-row
+        // order) go into this slot's buffers. The slot's previous item has finished: its
+        // consumers arrived on item_empty only after its last MMA completed.
+        item_work[slot] = w;
+        mbar_arrive_expect_tx(&q_full[slot], q_tx);
+        const uint32_t qdst = smem_u32(q_bufs + slot * q_buf_bytes);
+#pragma unroll
+        for (int ch = 0; ch < KvStage<D>::kPanels; ++ch)
+          tma_load_3d(qdst + ch * (16 * 128), q_map, ch * 64, w.h * p.group, w.q0 + w.row0 / p.group, &q_full[slot]);
+      }
       mbar_arrive(&item_full[slot]);
     }
     if (idx >= p.num_items) {
@@ -354,7 +369,7 @@ template <int D, int STAGES>
 __device__ __forceinline__ void producer_follow_v(const FwdParams& p, const KvMaps& maps, uint8_t* stages,
                                                   uint64_t* full, uint64_t* empty, uint64_t* item_full,
                                                   uint64_t* item_empty, const int* item_slot,
-                                                  volatile int* abort_flag, int lane) {
+                                                  const Work* item_work, volatile int* abort_flag, int lane) {
   const uint64_t policy = l2_policy_evict_first();
   const int groups = kBN / p.box_rows;
   const bool lane_per_group = groups <= 32;
@@ -364,7 +379,7 @@ __device__ __forceinline__ void producer_follow_v(const FwdParams& p, const KvMa
     if (!mbar_wait(&item_full[slot], (k >> 1) & 1, abort_flag, p.err, kDevErrTimeoutProducer)) return;
     const int idx = item_slot[slot];
     if (idx >= p.num_items) return;
-    const Work w = get_work(p, idx);
+    const Work w = item_work[slot];
     GroupSrc cur{}, nxt{};
     if (lane_per_group && lane < groups && w.tile_begin < w.tile_end) cur = resolve_group(p, w, w.tile_begin, lane);
     for (int t = w.tile_begin; t < w.tile_end; ++t, ++c) {
@@ -488,7 +503,7 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 // Device-side launch helpers live in the per-kernel .cu files.
 template <int D>
-cudaError_t launch_decode(const FwdParams& p, const KvMaps& maps, int grid, cudaStream_t s);
+cudaError_t launch_decode(const FwdParams& p, const KvMaps& maps, const CUtensorMap& q_map, int grid, cudaStream_t s);
 template <int D>
 cudaError_t launch_prefill(const FwdParams& p, const KvMaps& maps, int grid, cudaStream_t s);
 template <int D>

@@ -13,6 +13,9 @@
 //
 // Warp roles (224 threads): warp 0 = TMA producer of K (and the item scheduler), warp 6 =
 // TMA producer of V, warp 1 = MMA issuer + TMEM owner, warps 2-5 = softmax / epilogue.
+// Producer warp 0 also publishes each item's descriptor in shared memory and loads its Q
+// rows by TMA into a per-item-slot buffer, ahead of time: an item boundary then costs no
+// global-memory round trip on the consumer side.
 #include <cmath>
 
 #include "tfa_common.cuh"
@@ -40,15 +43,16 @@ struct DecodeCfg {
   static constexpr int kStageBytes = KvStage<D>::kBytes;
   static constexpr int kQBytes = kPanels * kNP * 128;  // Q: kNP rows x D, K-major SW128 panels
   static constexpr int kPBytes = 2 * kNP * 128;        // P^T: kNP rows x 128 tokens (2 panels)
-  static constexpr int kQOff = kStages * kStageBytes;
-  static constexpr int kPOff = kQOff + kQBytes;          // two P buffers
+  static constexpr int kQOff = kStages * kStageBytes;    // two Q buffers (one per item slot)
+  static constexpr int kPOff = kQOff + 2 * kQBytes;      // two P buffers
   static constexpr int kDynBytes = kPOff + 2 * kPBytes + 1024;  // + alignment slack
   static constexpr uint32_t kTmemCols = 64;              // S^T x2 (16 cols), O^T x2 (16 cols)
 };
 
 template <int D>
 __global__ void __launch_bounds__(224, 1)
-    decode_kernel(const __grid_constant__ FwdParams p, const __grid_constant__ KvMaps maps) {
+    decode_kernel(const __grid_constant__ FwdParams p, const __grid_constant__ KvMaps maps,
+                  const __grid_constant__ CUtensorMap q_map) {
   using Cfg = DecodeCfg<D>;
   extern __shared__ uint8_t dyn_smem[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dyn_smem) + 1023) & ~uintptr_t(1023));
@@ -60,6 +64,7 @@ __global__ void __launch_bounds__(224, 1)
   __shared__ uint64_t s_full[2], s_free[2], p_full[2], o_full[2], o_free[2];
   __shared__ uint64_t item_full[2], item_empty[2], q_full[2], red_bar;
   __shared__ int item_slot[2];
+  __shared__ Work item_work[2];
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_flag;
   __shared__ __align__(16) float red_max[2][4][kNP];
@@ -83,7 +88,7 @@ __global__ void __launch_bounds__(224, 1)
       mbar_init(&o_free[i], 4);
       mbar_init(&item_full[i], 1);
       mbar_init(&item_empty[i], 6);
-      mbar_init(&q_full[i], 4);
+      mbar_init(&q_full[i], 1);
     }
     mbar_init(&red_bar, 4);
     abort_flag = 0;
@@ -92,6 +97,7 @@ __global__ void __launch_bounds__(224, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&maps.k_box);
     tma_prefetch_desc(&maps.v_box);
+    tma_prefetch_desc(&q_map);
   }
   if (warp == 1) tmem_alloc(&tmem_base_sh, Cfg::kTmemCols);
   tc_fence_before();
@@ -103,15 +109,15 @@ __global__ void __launch_bounds__(224, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    producer_loop<D, Cfg::kStages>(p, maps, stages, full, empty, item_full, item_empty, item_slot, &abort_flag,
-                                   lane);
+    producer_loop<D, Cfg::kStages>(p, maps, stages, full, empty, item_full, item_empty, item_slot, item_work, &q_map,
+                                   q_smem, Cfg::kQBytes, q_full, &abort_flag, lane);
   } else if (warp == 6) {
-    producer_follow_v<D, Cfg::kStages>(p, maps, stages, full, empty, item_full, item_empty, item_slot, &abort_flag, lane);
+    producer_follow_v<D, Cfg::kStages>(p, maps, stages, full, empty, item_full, item_empty, item_slot, item_work,
+                                       &abort_flag, lane);
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     const uint32_t idesc_qk = make_idesc_bf16_f32(128, kNP, false, false);
     const uint32_t idesc_pv = make_idesc_bf16_f32(128, kNP, true, false);
-    const uint32_t q_addr = smem_u32(q_smem);
     int c = 0;
     bool ok = true;
     for (int k = 0; ok; ++k) {
@@ -119,8 +125,9 @@ __global__ void __launch_bounds__(224, 1)
       if (!mbar_wait(&item_full[slot], (k >> 1) & 1, &abort_flag, p.err, kDevErrTimeoutMma)) break;
       const int idx = item_slot[slot];
       if (idx >= p.num_items) break;
-      const Work w = get_work(p, idx);
+      const Work w = item_work[slot];
       const int n = w.tile_end - w.tile_begin;
+      const uint32_t q_addr = smem_u32(q_smem + slot * Cfg::kQBytes);
       if (!mbar_wait(&q_full[slot], (k >> 1) & 1, &abort_flag, p.err, kDevErrTimeoutMma)) break;
       if (lane == 0 && k == 0) STAMP(4);
       if (lane == 0 && n > 0) {
@@ -228,28 +235,8 @@ __global__ void __launch_bounds__(224, 1)
       if (warp == 2 && lane == 0 && k == 0) STAMP(6);
       const int idx = item_slot[slot];
       if (idx >= p.num_items) break;
-      const Work w = get_work(p, idx);
+      const Work w = item_work[slot];
       const int n = w.tile_end - w.tile_begin;
-
-      // Q rows -> shared memory (K-major, 128-byte swizzle); rows >= nrows are zero.
-      {
-        const int r = tq >> 3, u = tq & 7;
-#pragma unroll
-        for (int ch = 0; ch < Cfg::kPanels; ++ch) {
-          uint4 val = make_uint4(0, 0, 0, 0);
-          if (r < w.nrows) {
-            const int R = w.row0 + r;
-            const __nv_bfloat16* src = p.q + (int64_t)(w.q0 + R / p.group) * p.q_s0 +
-                                       (int64_t)(w.h * p.group + R % p.group) * p.q_s1 + ch * 64 + u * 8;
-            val = __ldg(reinterpret_cast<const uint4*>(src));
-          }
-          *reinterpret_cast<uint4*>(q_smem + ch * (kNP * 128) + r * 128 + ((u ^ (r & 7)) << 4)) = val;
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&q_full[slot]);
-        if (warp == 2 && lane == 0 && k == 0) STAMP(7);
-      }
 
       // Per-row constants, computed by lane r for row r and broadcast: visible kv range,
       // and where the row's output goes.
@@ -454,7 +441,7 @@ int decode_smem_bytes() {
 }
 
 template <int D>
-cudaError_t launch_decode(const FwdParams& p, const KvMaps& maps, int grid, cudaStream_t s) {
+cudaError_t launch_decode(const FwdParams& p, const KvMaps& maps, const CUtensorMap& q_map, int grid, cudaStream_t s) {
   static bool configured[128] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -465,7 +452,7 @@ cudaError_t launch_decode(const FwdParams& p, const KvMaps& maps, int grid, cuda
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
-  decode_kernel<D><<<grid, 224, DecodeCfg<D>::kDynBytes, s>>>(p, maps);
+  decode_kernel<D><<<grid, 224, DecodeCfg<D>::kDynBytes, s>>>(p, maps, q_map);
   return cudaGetLastError();
 }
 
@@ -477,7 +464,8 @@ extern "C" __attribute__((visibility("default"))) int tfa_decode_stamps_read(uns
 
 template int decode_smem_bytes<64>();
 template int decode_smem_bytes<128>();
-template cudaError_t launch_decode<64>(const FwdParams&, const KvMaps&, int, cudaStream_t);
-template cudaError_t launch_decode<128>(const FwdParams&, const KvMaps&, int, cudaStream_t);
+template cudaError_t launch_decode<64>(const FwdParams&, const KvMaps&, const CUtensorMap&, int, cudaStream_t);
+template cudaError_t launch_decode<128>(const FwdParams&, const KvMaps&, const CUtensorMap&, int,
+                                              cudaStream_t);
 
 }  // namespace tfa

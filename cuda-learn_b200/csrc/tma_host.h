@@ -50,4 +50,24 @@ inline int encode_kv_map(CUtensorMap* map, const void* base, int64_t num_blocks,
   return (int)r;
 }
 
+// Query rows for the decode kernel: q is [total_q, num_q_heads, head_dim] bf16 with
+// element strides (token, head) and a contiguous head_dim. The map is 3-D, innermost
+// first (head_dim, q_head, token); a box is (64 columns, group heads, tokens) and lands
+// as group * tokens rows of 128 bytes (row = token * group + head, the packed-row order)
+// with the 128-byte swizzle, the K-major SW128 operand layout of the MMA. Tokens past
+// total_q are zero-filled.
+inline int encode_q_map(CUtensorMap* map, const void* base, int64_t total_q, int64_t num_q_heads, int64_t head_dim,
+                        int64_t token_stride, int64_t head_stride, uint32_t group, uint32_t tokens) {
+  auto fn = get_encode_tiled();
+  if (!fn) return -1;
+  cuuint64_t dims[3] = {(cuuint64_t)head_dim, (cuuint64_t)num_q_heads, (cuuint64_t)total_q};
+  cuuint64_t strides[2] = {(cuuint64_t)head_stride * 2, (cuuint64_t)token_stride * 2};
+  cuuint32_t box[3] = {64, group, tokens};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return (int)r;
+}
+
 }  // namespace tfa
