@@ -237,12 +237,13 @@ __device__ __forceinline__ void issue_group(const FwdParams& p, const KvMaps& ma
   }
 }
 
-// Boxes of one group of one tensor (tensor 1 = K, 0 = V) into its half of `stage`.
+// Boxes of one group of one tensor (tensor 1 = K, 0 = V) into `half`, one tile of that
+// tensor (kPanels panels of 128 rows).
 template <int D>
 __device__ __forceinline__ void issue_group_one(const FwdParams& p, const KvMaps& maps, const Work& w, int g,
-                                                GroupSrc src, int tensor, uint8_t* stage, uint64_t* full_bar,
+                                                GroupSrc src, int tensor, uint8_t* half, uint64_t* full_bar,
                                                 uint64_t policy) {
-  const uint32_t dst = smem_u32(stage) + g * p.box_rows * 128 + tensor * KvStage<D>::kTensorBytes;
+  const uint32_t dst = smem_u32(half) + g * p.box_rows * 128;
   const CUtensorMap* box = tensor ? &maps.k_box : &maps.v_box;
   if (src.valid == p.box_rows && src.page >= 0 && src.page < p.num_blocks) {
 #pragma unroll
@@ -277,7 +278,7 @@ __device__ void decode_stamp_hook(int i);
 // of the current one waits for its stage. The first item of CTA i is item i; later items
 // come from the shared counter offset by the grid size, so start-up has no atomic.
 template <int D, int STAGES>
-__device__ __forceinline__ void producer_loop(const FwdParams& p, const KvMaps& maps, uint8_t* stages,
+__device__ __forceinline__ void producer_loop(const FwdParams& p, const KvMaps& maps, uint8_t* ring,
                                               uint64_t* full, uint64_t* empty, uint64_t* item_full,
                                               uint64_t* item_empty, int* item_slot, Work* item_work,
                                               const CUtensorMap* q_map, uint8_t* q_bufs, int q_buf_bytes,
@@ -340,7 +341,7 @@ __device__ __forceinline__ void producer_loop(const FwdParams& p, const KvMaps& 
         if (!mbar_wait(&empty[st], ((c / STAGES) & 1) ^ 1, abort_flag, p.err, kDevErrTimeoutProducer)) return;
         if (lane == 0) mbar_arrive_expect_tx(&full[st], KvStage<D>::kTensorBytes);
         __syncwarp();
-        if (lane < groups) issue_group_one<D>(p, maps, w, lane, cur, 1, stages + st * KvStage<D>::kBytes, &full[st], policy);
+        if (lane < groups) issue_group_one<D>(p, maps, w, lane, cur, 1, ring + st * KvStage<D>::kTensorBytes, &full[st], policy);
 #ifdef TFA_PROFILE
         if (lane == 0 && c == 0 && blockIdx.x == 0 && p.rows_per_tile == 16) decode_stamp_hook(3);
 #endif
@@ -354,7 +355,7 @@ __device__ __forceinline__ void producer_loop(const FwdParams& p, const KvMaps& 
         if (lane == 0) mbar_arrive_expect_tx(&full[st], KvStage<D>::kTensorBytes);
         __syncwarp();
         for (int g = lane; g < groups; g += 32)
-          issue_group_one<D>(p, maps, w, g, resolve_group(p, w, t, g), 1, stages + st * KvStage<D>::kBytes, &full[st],
+          issue_group_one<D>(p, maps, w, g, resolve_group(p, w, t, g), 1, ring + st * KvStage<D>::kTensorBytes, &full[st],
                              policy);
       }
     }
@@ -362,11 +363,11 @@ __device__ __forceinline__ void producer_loop(const FwdParams& p, const KvMaps& 
 }
 
 // Second producer warp of the decode kernel: follows the item queue like a consumer and
-// requests the V half of every stage (the first producer requests the K half), so the two
-// warps' barrier waits and loop overhead overlap each other's TMA issue. Each stage's
-// full barrier therefore expects two arrivals.
+// fills the ring of V tiles (the first producer fills the ring of K tiles), so the two
+// warps' barrier waits and loop overhead overlap each other's TMA issue. The rings have
+// their own barriers: a K slot is free again once QK has read it, a V slot after P.V.
 template <int D, int STAGES>
-__device__ __forceinline__ void producer_follow_v(const FwdParams& p, const KvMaps& maps, uint8_t* stages,
+__device__ __forceinline__ void producer_follow_v(const FwdParams& p, const KvMaps& maps, uint8_t* ring,
                                                   uint64_t* full, uint64_t* empty, uint64_t* item_full,
                                                   uint64_t* item_empty, const int* item_slot,
                                                   const Work* item_work, volatile int* abort_flag, int lane) {
@@ -389,10 +390,10 @@ __device__ __forceinline__ void producer_follow_v(const FwdParams& p, const KvMa
       if (lane == 0) mbar_arrive_expect_tx(&full[st], KvStage<D>::kTensorBytes);
       __syncwarp();
       if (lane_per_group) {
-        if (lane < groups) issue_group_one<D>(p, maps, w, lane, cur, 0, stages + st * KvStage<D>::kBytes, &full[st], policy);
+        if (lane < groups) issue_group_one<D>(p, maps, w, lane, cur, 0, ring + st * KvStage<D>::kTensorBytes, &full[st], policy);
       } else {
         for (int g = lane; g < groups; g += 32)
-          issue_group_one<D>(p, maps, w, g, resolve_group(p, w, t, g), 0, stages + st * KvStage<D>::kBytes, &full[st],
+          issue_group_one<D>(p, maps, w, g, resolve_group(p, w, t, g), 0, ring + st * KvStage<D>::kTensorBytes, &full[st],
                              policy);
       }
       cur = nxt;

@@ -20,6 +20,13 @@
 
 #include "tfa_common.cuh"
 
+#ifndef TFA_DECODE_KSLOTS
+#define TFA_DECODE_KSLOTS 3
+#endif
+#ifndef TFA_DECODE_VSLOTS
+#define TFA_DECODE_VSLOTS 3
+#endif
+
 namespace tfa {
 
 namespace {
@@ -39,11 +46,19 @@ namespace {
 template <int D>
 struct DecodeCfg {
   static constexpr int kPanels = D / 64;
-  static constexpr int kStages = (D == 128) ? 3 : 6;
-  static constexpr int kStageBytes = KvStage<D>::kBytes;
+  // K and V tiles live in separate rings: a K slot is released as soon as QK has read
+  // it, a V slot only after the tile's softmax and P.V, so the V ring holds its tiles longer
+  static constexpr int kKSlots = (D == 128) ? TFA_DECODE_KSLOTS : 6;
+  static constexpr int kVSlots = (D == 128) ? TFA_DECODE_VSLOTS : 6;
+  static constexpr int kTileBytes = KvStage<D>::kTensorBytes;  // one K or V tile
+  // V ring first: the P.V MMA always spans M = 128 head-dim rows, so for D = 64 its upper
+  // 64 rows read the 16 KB after the V tile (their output rows are never used). With the
+  // V ring first that read stays inside this CTA's shared memory (next V slot / K ring).
+  static constexpr int kVOff = 0;
+  static constexpr int kKOff = kVSlots * kTileBytes;
   static constexpr int kQBytes = kPanels * kNP * 128;  // Q: kNP rows x D, K-major SW128 panels
   static constexpr int kPBytes = 2 * kNP * 128;        // P^T: kNP rows x 128 tokens (2 panels)
-  static constexpr int kQOff = kStages * kStageBytes;    // two Q buffers (one per item slot)
+  static constexpr int kQOff = kKOff + kKSlots * kTileBytes;  // two Q buffers (one per item slot)
   static constexpr int kPOff = kQOff + 2 * kQBytes;      // two P buffers
   static constexpr int kDynBytes = kPOff + 2 * kPBytes + 1024;  // + alignment slack
   static constexpr uint32_t kTmemCols = 64;              // S^T x2 (16 cols), O^T x2 (16 cols)
@@ -56,11 +71,12 @@ __global__ void __launch_bounds__(224, 1)
   using Cfg = DecodeCfg<D>;
   extern __shared__ uint8_t dyn_smem[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dyn_smem) + 1023) & ~uintptr_t(1023));
-  uint8_t* stages = smem;
+  uint8_t* k_ring = smem + Cfg::kKOff;
+  uint8_t* v_ring = smem + Cfg::kVOff;
   uint8_t* q_smem = smem + Cfg::kQOff;
   uint8_t* p_smem = smem + Cfg::kPOff;
 
-  __shared__ uint64_t full[Cfg::kStages], empty[Cfg::kStages];
+  __shared__ uint64_t full_k[Cfg::kKSlots], empty_k[Cfg::kKSlots], full_v[Cfg::kVSlots], empty_v[Cfg::kVSlots];
   __shared__ uint64_t s_full[2], s_free[2], p_full[2], o_full[2], o_free[2];
   __shared__ uint64_t item_full[2], item_empty[2], q_full[2], red_bar;
   __shared__ int item_slot[2];
@@ -76,9 +92,13 @@ __global__ void __launch_bounds__(224, 1)
   if (tid == 0) STAMP(0);
 
   if (tid == 0) {
-    for (int i = 0; i < Cfg::kStages; ++i) {
-      mbar_init(&full[i], 2);  // K and V producers
-      mbar_init(&empty[i], 1);
+    for (int i = 0; i < Cfg::kKSlots; ++i) {
+      mbar_init(&full_k[i], 1);
+      mbar_init(&empty_k[i], 1);
+    }
+    for (int i = 0; i < Cfg::kVSlots; ++i) {
+      mbar_init(&full_v[i], 1);
+      mbar_init(&empty_v[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
@@ -109,10 +129,10 @@ __global__ void __launch_bounds__(224, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    producer_loop<D, Cfg::kStages>(p, maps, stages, full, empty, item_full, item_empty, item_slot, item_work, &q_map,
+    producer_loop<D, Cfg::kKSlots>(p, maps, k_ring, full_k, empty_k, item_full, item_empty, item_slot, item_work, &q_map,
                                    q_smem, Cfg::kQBytes, q_full, &abort_flag, lane);
   } else if (warp == 6) {
-    producer_follow_v<D, Cfg::kStages>(p, maps, stages, full, empty, item_full, item_empty, item_slot, item_work,
+    producer_follow_v<D, Cfg::kVSlots>(p, maps, v_ring, full_v, empty_v, item_full, item_empty, item_slot, item_work,
                                        &abort_flag, lane);
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -132,9 +152,9 @@ __global__ void __launch_bounds__(224, 1)
       if (lane == 0 && k == 0) STAMP(4);
       if (lane == 0 && n > 0) {
         auto issue_qk = [&](int cc) {
-          const int st = cc % Cfg::kStages;
+          const int st = cc % Cfg::kKSlots;
           tc_fence_after();
-          const uint32_t k_addr = smem_u32(stages + st * Cfg::kStageBytes) + KvStage<D>::kTensorBytes;
+          const uint32_t k_addr = smem_u32(k_ring + st * Cfg::kTileBytes);
           const uint32_t d_tmem = tmem + (cc & 1) * kNP;
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
@@ -143,12 +163,13 @@ __global__ void __launch_bounds__(224, 1)
             umma_bf16_ss(d_tmem, make_sdesc_sw128(k_addr + off, 16, 1024), make_sdesc_sw128(q_addr + qoff, 16, 1024),
                          idesc_qk, kk > 0 ? 1u : 0u);
           }
+          umma_commit(&empty_k[st]);  // frees the K slot once QK has read it
           umma_commit(&s_full[cc & 1]);
         };
         auto issue_pv = [&](int cj) {
           tc_fence_after();
-          const int st = cj % Cfg::kStages;
-          const uint32_t v_addr = smem_u32(stages + st * Cfg::kStageBytes);
+          const int st = cj % Cfg::kVSlots;
+          const uint32_t v_addr = smem_u32(v_ring + st * Cfg::kTileBytes);
           const uint32_t pb = smem_u32(p_smem + (cj & 1) * Cfg::kPBytes);
           const uint32_t d_tmem = tmem + 32 + (cj & 1) * kNP;
 #pragma unroll
@@ -158,7 +179,7 @@ __global__ void __launch_bounds__(224, 1)
             umma_bf16_ss(d_tmem, make_sdesc_sw128(v_addr + voff, KvStage<D>::kPanelBytes, 1024),
                          make_sdesc_sw128(pb + poff, 16, 1024), idesc_pv, kk > 0 ? 1u : 0u);
           }
-          umma_commit(&empty[st]);  // frees the K/V stage once this P.V (and all before it) completes
+          umma_commit(&empty_v[st]);  // frees the V slot once this P.V has read it
           umma_commit(&o_full[cj & 1]);
         };
         // QK of tile jq and P.V of tile jp are issued as soon as each one's inputs are
@@ -172,7 +193,7 @@ __global__ void __launch_bounds__(224, 1)
           bool progress = false;
           if (jq < n && jq < jp + 2) {
             const int cq = c + jq;
-            if (mbar_test(&full[cq % Cfg::kStages], (cq / Cfg::kStages) & 1) &&
+            if (mbar_test(&full_k[cq % Cfg::kKSlots], (cq / Cfg::kKSlots) & 1) &&
                 mbar_test(&s_free[cq & 1], ((cq >> 1) & 1) ^ 1)) {
               issue_qk(cq);
               ++jq;
@@ -181,7 +202,8 @@ __global__ void __launch_bounds__(224, 1)
           }
           if (jp < jq) {
             const int cp = c + jp;
-            if (mbar_test(&p_full[cp & 1], (cp >> 1) & 1) && mbar_test(&o_free[cp & 1], ((cp >> 1) & 1) ^ 1)) {
+            if (mbar_test(&p_full[cp & 1], (cp >> 1) & 1) && mbar_test(&o_free[cp & 1], ((cp >> 1) & 1) ^ 1) &&
+                mbar_test(&full_v[cp % Cfg::kVSlots], (cp / Cfg::kVSlots) & 1)) {
               issue_pv(cp);
               ++jp;
               progress = true;
