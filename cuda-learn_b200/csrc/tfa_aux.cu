@@ -7,37 +7,9 @@ namespace tfa {
 
 namespace {
 
-// Restates the merge of v8's splitkv_combine_kernel (v8/flash_attn_func.cu:701-777):
-// out = sum_s 2^(lse_s - M) * o_s / sum_s 2^(lse_s - M), M = max_s lse_s, all in the
-// log2 domain of the scaled scores. One warp per (q token, q head); partial outputs are
-// already normalised per split. Only (token, head) pairs whose q tile was split run here;
-// the others were written directly by the attention kernel.
-template <int D>
-__global__ void __launch_bounds__(128) combine_kernel(const __grid_constant__ FwdParams p) {
-  constexpr int EPL = D / 32;  // elements per lane
-  grid_dependency_wait();      // partials of the attention kernel are complete and visible
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t pair = (int64_t)blockIdx.x * 4 + warp;
-  if (pair >= (int64_t)p.total_q * p.hq) return;
-  const int tok = (int)(pair / p.hq), qh = (int)(pair % p.hq);
-  int lo = 0, hi = p.batch - 1;
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (__ldg(p.cu_seqlens_q + mid) <= tok) lo = mid;
-    else hi = mid - 1;
-  }
-  const int b = lo;
-  const int q0 = __ldg(p.cu_seqlens_q + b);
-  const int q_len = __ldg(p.cu_seqlens_q + b + 1) - q0;
-  const int kv_len = __ldg(p.seqused_k + b);
-  const int R = (tok - q0) * p.group + qh % p.group;
-  const int row0 = (R / p.rows_per_tile) * p.rows_per_tile;
-  const int nrows = imin(p.rows_per_tile, q_len * p.group - row0);
-  int t_lo, n;
-  tile_span(p, q_len, kv_len, row0, nrows, t_lo, n);
-  const int ns = splits_for(p, n);
-  if (ns <= 1) return;
-
+// Merges the split partials of one (q token, q head) row into `out` (and the LSE).
+template <int D, int EPL>
+__device__ __forceinline__ void combine_row(const FwdParams& p, int64_t pair, int tok, int qh, int ns, int lane) {
   const int64_t stride = (int64_t)p.total_q * p.hq;
   __nv_bfloat16* dst = p.out + (int64_t)tok * p.o_s0 + (int64_t)qh * p.o_s1 + lane * EPL;
   float acc[EPL];
@@ -89,6 +61,31 @@ __global__ void __launch_bounds__(128) combine_kernel(const __grid_constant__ Fw
   if (lane == 0 && p.lse) p.lse[pair] = (mx + lg2_approx(wsum)) * kLn2;
 }
 
+// Restates the merge of v8's splitkv_combine_kernel (v8/flash_attn_func.cu:701-777):
+// out = sum_s 2^(lse_s - M) * o_s / sum_s 2^(lse_s - M), M = max_s lse_s, all in the
+// log2 domain of the scaled scores. One CTA per work group (q tile slot, sequence, kv
+// head; the attention kernels' item order with split 0), one warp per packed row of it;
+// partial outputs are already normalised per split. Groups that were not split were
+// written directly by the attention kernel and return at once. The group's geometry only
+// depends on the call's inputs, so it is computed before the wait for the attention
+// kernel (programmatic dependent launch), overlapping that kernel's tail.
+template <int D>
+__global__ void __launch_bounds__(128) combine_kernel(const __grid_constant__ FwdParams p) {
+  constexpr int EPL = D / 32;  // elements per lane
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const Work w = get_work(p, (int)blockIdx.x);
+  const int ns = w.nsplits;
+  if (ns <= 1 || w.nrows <= 0) return;
+  grid_dependency_wait();  // partials of the attention kernel are complete and visible
+  for (int r = warp; r < w.nrows; r += 4) {
+    const int R = w.row0 + r;
+    const int tok = w.q0 + R / p.group;
+    const int qh = w.h * p.group + R % p.group;
+    const int64_t pair = (int64_t)tok * p.hq + qh;
+    combine_row<D, EPL>(p, pair, tok, qh, ns, lane);
+  }
+}
+
 // One CTA per (kv tile, sequence, kv head): the producer warp stages the tile with the
 // attention kernels' TMA gather (produce_tile), then all threads copy the valid rows out.
 template <int D>
@@ -129,8 +126,7 @@ __global__ void __launch_bounds__(128) gather_kernel(const __grid_constant__ Fwd
 
 template <int D>
 cudaError_t launch_combine(const FwdParams& p, cudaStream_t s) {
-  const int64_t pairs = (int64_t)p.total_q * p.hq;
-  const int64_t blocks = (pairs + 3) / 4;
+  const int64_t blocks = (int64_t)p.q_tiles * p.batch * p.hkv;  // one CTA per work group
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)blocks);
   cfg.blockDim = dim3(128);
