@@ -1,5 +1,6 @@
 // C ABI of the paged attention forward (declared in include/tfa.h): argument checks,
 // split-KV planning, TMA descriptor encoding and kernel launches. Host code only.
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
@@ -290,7 +291,9 @@ int fwd_impl(const tfa_fwd_params* a, void* workspace, size_t workspace_bytes, v
   }
   if (ev_end && cudaEventRecord(reinterpret_cast<cudaEvent_t>(ev_end), s) != cudaSuccess) return TFA_ERR_CUDA;
   if (pl.combine) {
-    e = a->head_dim == 64 ? launch_combine<64>(p, s) : launch_combine<128>(p, s);
+    // packed rows per group: at most one q tile, at most the longest query times the group
+    const int64_t rows = std::min<int64_t>(pl.rows, a->max_seqlen_q * (a->num_q_heads / a->num_kv_heads));
+    e = a->head_dim == 64 ? launch_combine<64>(p, (int)rows, s) : launch_combine<128>(p, (int)rows, s);
     if (e != cudaSuccess) return TFA_ERR_CUDA;
   }
   return TFA_OK;

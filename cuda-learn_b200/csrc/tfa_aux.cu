@@ -64,20 +64,22 @@ __device__ __forceinline__ void combine_row(const FwdParams& p, int64_t pair, in
 // Restates the merge of v8's splitkv_combine_kernel (v8/flash_attn_func.cu:701-777):
 // out = sum_s 2^(lse_s - M) * o_s / sum_s 2^(lse_s - M), M = max_s lse_s, all in the
 // log2 domain of the scaled scores. One CTA per work group (q tile slot, sequence, kv
-// head; the attention kernels' item order with split 0), one warp per packed row of it;
+// head; the attention kernels' item order with split 0), one warp per packed row of it
+// (up to 16 warps, looping over larger groups);
 // partial outputs are already normalised per split. Groups that were not split were
 // written directly by the attention kernel and return at once. The group's geometry only
 // depends on the call's inputs, so it is computed before the wait for the attention
 // kernel (programmatic dependent launch), overlapping that kernel's tail.
 template <int D>
-__global__ void __launch_bounds__(128) combine_kernel(const __grid_constant__ FwdParams p) {
+__global__ void __launch_bounds__(512) combine_kernel(const __grid_constant__ FwdParams p) {
   constexpr int EPL = D / 32;  // elements per lane
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const Work w = get_work(p, (int)blockIdx.x);
   const int ns = w.nsplits;
   if (ns <= 1 || w.nrows <= 0) return;
   grid_dependency_wait();  // partials of the attention kernel are complete and visible
-  for (int r = warp; r < w.nrows; r += 4) {
+  const int nwarps = (int)(blockDim.x >> 5);
+  for (int r = warp; r < w.nrows; r += nwarps) {
     const int R = w.row0 + r;
     const int tok = w.q0 + R / p.group;
     const int qh = w.h * p.group + R % p.group;
@@ -125,11 +127,13 @@ __global__ void __launch_bounds__(128) gather_kernel(const __grid_constant__ Fwd
 }  // namespace
 
 template <int D>
-cudaError_t launch_combine(const FwdParams& p, cudaStream_t s) {
+cudaError_t launch_combine(const FwdParams& p, int max_rows, cudaStream_t s) {
   const int64_t blocks = (int64_t)p.q_tiles * p.batch * p.hkv;  // one CTA per work group
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)blocks);
-  cfg.blockDim = dim3(128);
+  // one warp per packed row of a group, up to 16
+  const int warps = max_rows < 1 ? 1 : (max_rows > 16 ? 16 : max_rows);
+  cfg.blockDim = dim3(32 * warps);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -159,8 +163,8 @@ cudaError_t launch_gather(const FwdParams& p, const KvMaps& maps, int max_tiles,
   return cudaGetLastError();
 }
 
-template cudaError_t launch_combine<64>(const FwdParams&, cudaStream_t);
-template cudaError_t launch_combine<128>(const FwdParams&, cudaStream_t);
+template cudaError_t launch_combine<64>(const FwdParams&, int, cudaStream_t);
+template cudaError_t launch_combine<128>(const FwdParams&, int, cudaStream_t);
 template cudaError_t launch_gather<64>(const FwdParams&, const KvMaps&, int, const int64_t*, void*, void*,
                                        cudaStream_t);
 template cudaError_t launch_gather<128>(const FwdParams&, const KvMaps&, int, const int64_t*, void*, void*,

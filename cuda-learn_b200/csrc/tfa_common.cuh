@@ -508,7 +508,7 @@ cudaError_t launch_decode(const FwdParams& p, const KvMaps& maps, const CUtensor
 template <int D>
 cudaError_t launch_prefill(const FwdParams& p, const KvMaps& maps, int grid, cudaStream_t s);
 template <int D>
-cudaError_t launch_combine(const FwdParams& p, cudaStream_t s);
+cudaError_t launch_combine(const FwdParams& p, int max_rows, cudaStream_t s);
 template <int D>
 cudaError_t launch_gather(const FwdParams& p, const KvMaps& maps, int max_tiles, const int64_t* kv_offsets,
                           void* k_out, void* v_out, cudaStream_t s);
