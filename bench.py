@@ -39,7 +39,7 @@ UNIT = "TB/s"
 L2_BYTES = 126 * 1024 * 1024
 # DRAM bytes (read + write) of one decode_kernel launch per algorithmic K/V byte, from the
 # ncu capture summarised in profiles/decode_kernel_C5.md (reduced C5, scaled by K/V bytes).
-TRAFFIC_PER_KV_BYTE = (471.89e6 + 3.62e6) / 471.49e6
+TRAFFIC_PER_KV_BYTE = (471.89e6 + 6.53e6) / 471.49e6
 
 
 def parse_args():
