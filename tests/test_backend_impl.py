@@ -228,3 +228,23 @@ def test_dump_and_replay_cuda_path(monkeypatch, tmp_path):
     assert torch.equal(again, dumped)  # same inputs, same plan: bit-identical
     ref = _oracle(case, None)
     assert (again.float().cpu() - ref).abs().max().item() <= OUT_TOL
+
+
+# ------------------------------------------------------------------ vLLM e2e script (CPU parts)
+def test_vllm_e2e_compare_and_prompts():
+    from toy_flash_attn import vllm_e2e
+
+    prompts = vllm_e2e._prompts(4, vllm_e2e.QWEN2_SMALL["vocab_size"])
+    assert [len(p) for p in prompts] == [17, 54, 91, 128]
+    assert all(0 <= t < vllm_e2e.QWEN2_SMALL["vocab_size"] for p in prompts for t in p)
+    cfg = vllm_e2e.QWEN2_SMALL
+    assert cfg["num_attention_heads"] % cfg["num_key_value_heads"] == 0
+    assert cfg["hidden_size"] // cfg["num_attention_heads"] == 64  # a head size the kernels take
+    a = {"sequences": [{"tokens": [1, 2, 3, 4], "logprobs": [-1.0, -2.0, -3.0, -4.0]},
+                       {"tokens": [5, 6], "logprobs": [-0.5, -0.25]}]}
+    b = {"sequences": [{"tokens": [1, 2, 9, 4], "logprobs": [-1.0, -2.5, -3.0, -4.0]},
+                       {"tokens": [5, 6], "logprobs": [-0.5, -0.25]}]}
+    res = vllm_e2e.compare(a, b)
+    assert res["first_divergence"] == [2, 2]
+    assert res["tokens_identical_prefix"] == 4 and res["tokens_total"] == 6
+    assert res["max_logprob_gap_before_divergence"] == 0.5
