@@ -107,6 +107,14 @@ int make_plan(const tfa_fwd_params* p, int device, Plan* pl) {
   } else {
     const int64_t est = (int64_t)p->batch * p->num_kv_heads * pl->q_tiles * tiles;
     cap = (est + 2 * sms - 1) / (2 * sms);
+    // Large decode calls: finer splits shorten the tail of the persistent grid (decode
+    // items are cheap to start). est counts every sequence at max_seqlen_k, so aim at ~16
+    // items per SM of that bound, but keep items of at least 16 tiles.
+    if (decode) {
+      int64_t fine = (est + 16 * sms - 1) / (16 * sms);
+      if (fine < 16) fine = 16;
+      if (fine < cap) cap = fine;
+    }
     if (cap < 1) cap = 1;
     if (cap > 64) cap = 64;
     S = (tiles + cap - 1) / cap;
