@@ -287,14 +287,16 @@ __global__ void __launch_bounds__(320, 1)
           }
           m_ref = tmax;
         }
-        // the previous P.V of this q tile must be complete before O is rescaled or P rewritten
-        if (j > 0) {
+        // Rescaling O needs the previous P.V of this q tile complete. Writing P needs no
+        // wait: P(j) overwrites only S(j), and the MMA warp issued QK(j) after P.V(j-1),
+        // which read P(j-1) from those columns, had completed.
+        if (j > 0 && __any_sync(0xffffffffu, rescale)) {
           if (!PROF_WAIT(1, mbar_wait(&o_full[x], (ts - 1) & 1, &abort_flag, p.err, kDevErrTimeoutSoftmax))) {
             ok = false;
             break;
           }
           tc_fence_after();
-          if (__any_sync(0xffffffffu, rescale)) {
+          {
 #pragma unroll 1
             for (int cc = 0; cc < D / 32; ++cc) {
               float t[32];
