@@ -15,7 +15,7 @@
 namespace tfa {
 namespace {
 
-constexpr size_t kCtrlBytes = 256;  // workspace control block: sched[2], err
+constexpr size_t kCtrlBytes = 256;  // workspace control block: sched[2], err, decode sched[2] at 4-5
 constexpr int kMaxDevices = 128;
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -70,7 +70,7 @@ struct Plan {
   size_t ws_bytes;
 };
 
-int make_plan(const tfa_fwd_params* p, int device, Plan* pl) {
+int make_plan_one(const tfa_fwd_params* p, int device, Plan* pl) {
   const int64_t G = p->num_q_heads / p->num_kv_heads;
   const bool decode = p->max_seqlen_q * G <= 16;
   pl->kernel = decode ? 0 : 1;
@@ -135,6 +135,39 @@ int make_plan(const tfa_fwd_params* p, int device, Plan* pl) {
     ws += rows * p->head_dim * sizeof(float);
   }
   pl->ws_bytes = ws;
+  return TFA_OK;
+}
+
+// The plan of a whole call. A call that needs the prefill kernel but may also hold
+// decode-shaped sequences (several sequences, GQA group <= 16: vLLM's chunked prefill mixes
+// decode tokens and prompt chunks in one batch) runs both kernels, each on its own kind of
+// sequence (FwdParams::seq_filter): decode-shaped sequences then stream at the decode
+// kernel's rate instead of occupying 128-row prefill tiles. Workspace: the prefill part
+// (the call's control block first), then the decode part's split buffers.
+constexpr int64_t kMixedMinBatch = 8;
+
+struct FullPlan {
+  Plan pre;  // the only plan unless mixed
+  Plan dec;  // mixed: the decode kernel's plan
+  int mixed;
+  size_t dec_off;  // mixed: byte offset of the decode part of the workspace
+  size_t ws_bytes;
+};
+
+int make_plan(const tfa_fwd_params* p, int device, FullPlan* fp) {
+  int rc = make_plan_one(p, device, &fp->pre);
+  if (rc != TFA_OK) return rc;
+  const int64_t G = p->num_q_heads / p->num_kv_heads;
+  fp->mixed = (fp->pre.kernel == 1 && p->batch >= kMixedMinBatch && G <= 16) ? 1 : 0;
+  fp->dec_off = 0;
+  fp->ws_bytes = fp->pre.ws_bytes;
+  if (fp->mixed) {
+    tfa_fwd_params d = *p;
+    d.max_seqlen_q = 16 / G;  // the decode kernel's sequences are at most this long
+    if ((rc = make_plan_one(&d, device, &fp->dec)) != TFA_OK) return rc;
+    fp->dec_off = align_up(fp->pre.ws_bytes, 256);
+    fp->ws_bytes = fp->dec_off + fp->dec.ws_bytes;
+  }
   return TFA_OK;
 }
 
@@ -239,10 +272,11 @@ int tfa_plan(const tfa_fwd_params* p, int device, tfa_plan_info* info) {
   if (!info) return TFA_ERR_NULL_POINTER;
   int rc = validate(p);
   if (rc != TFA_OK) return rc;
-  Plan pl;
-  rc = make_plan(p, device, &pl);
+  FullPlan fp;
+  rc = make_plan(p, device, &fp);
   if (rc != TFA_OK) return rc;
-  info->kernel = pl.kernel;
+  const Plan& pl = fp.pre;
+  info->kernel = fp.mixed ? 2 : pl.kernel;
   info->rows_per_tile = pl.rows;
   info->q_tiles = pl.q_tiles;
   info->max_splits = pl.max_splits;
@@ -250,15 +284,15 @@ int tfa_plan(const tfa_fwd_params* p, int device, tfa_plan_info* info) {
   info->num_items = pl.num_items;
   info->grid = pl.grid;
   info->combine = pl.combine;
-  info->workspace_bytes = pl.ws_bytes;
+  info->workspace_bytes = fp.ws_bytes;
   return TFA_OK;
 }
 
 size_t tfa_workspace_size(const tfa_fwd_params* p, int device) {
   if (validate(p) != TFA_OK) return 0;
-  Plan pl;
-  if (make_plan(p, device, &pl) != TFA_OK) return 0;
-  return pl.ws_bytes;
+  FullPlan fp;
+  if (make_plan(p, device, &fp) != TFA_OK) return 0;
+  return fp.ws_bytes;
 }
 
 }  // extern "C"
@@ -273,36 +307,60 @@ int fwd_impl(const tfa_fwd_params* a, void* workspace, size_t workspace_bytes, v
   int dev = 0;
   if ((rc = current_device(&dev)) != TFA_OK) return rc;
   if ((rc = check_device(dev)) != TFA_OK) return rc;
-  Plan pl;
-  if ((rc = make_plan(a, dev, &pl)) != TFA_OK) return rc;
-  if (!workspace || workspace_bytes < pl.ws_bytes || !aligned16(workspace)) return TFA_ERR_WORKSPACE;
+  FullPlan fp;
+  if ((rc = make_plan(a, dev, &fp)) != TFA_OK) return rc;
+  if (!workspace || workspace_bytes < fp.ws_bytes || !aligned16(workspace)) return TFA_ERR_WORKSPACE;
+  const Plan& pl = fp.pre;
   FwdParams p;
   fill_params(a, pl, workspace, &p);
+  FwdParams pd;  // mixed calls: the decode kernel's part
+  if (fp.mixed) {
+    fill_params(a, fp.dec, reinterpret_cast<uint8_t*>(workspace) + fp.dec_off, &pd);
+    // One control block per call (the first 256 bytes, always left zeroed): the decode
+    // kernel's scheduler counters are its words 4-5, the error word is shared.
+    pd.sched = p.sched + 4;
+    pd.err = p.err;
+    p.seq_filter = 2;
+    pd.seq_filter = 1;
+  }
   KvMaps maps;
   if ((rc = encode_maps(a, p.box_rows, &maps)) != TFA_OK) return rc;
+  const bool any_decode = pl.kernel == 0 || fp.mixed;
   CUtensorMap q_map;  // decode kernel only: (64 columns, group heads, 16 / group tokens) boxes of q
   std::memset(&q_map, 0, sizeof(q_map));
-  if (pl.kernel == 0 &&
+  if (any_decode &&
       encode_q_map(&q_map, a->q, a->total_q, a->num_q_heads, a->head_dim, a->q_stride[0], a->q_stride[1],
                    (uint32_t)p.group, (uint32_t)(16 / p.group)) != 0)
     return TFA_ERR_TENSOR_MAP;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  cudaError_t e;
+  cudaError_t e = cudaSuccess;
+  auto fail = [&](cudaError_t err) {
+    if (std::getenv("TFA_DEBUG")) std::fprintf(stderr, "tfa_fwd: launch failed: %s\n", cudaGetErrorString(err));
+    return TFA_ERR_CUDA;
+  };
   if (ev_begin && cudaEventRecord(reinterpret_cast<cudaEvent_t>(ev_begin), s) != cudaSuccess) return TFA_ERR_CUDA;
+  if (fp.mixed) {
+    e = a->head_dim == 64 ? launch_decode<64>(pd, maps, q_map, fp.dec.grid, s)
+                          : launch_decode<128>(pd, maps, q_map, fp.dec.grid, s);
+    if (e != cudaSuccess) return fail(e);
+  }
   if (a->head_dim == 64)
     e = pl.kernel == 0 ? launch_decode<64>(p, maps, q_map, pl.grid, s) : launch_prefill<64>(p, maps, pl.grid, s);
   else
     e = pl.kernel == 0 ? launch_decode<128>(p, maps, q_map, pl.grid, s) : launch_prefill<128>(p, maps, pl.grid, s);
-  if (e != cudaSuccess) {
-    if (std::getenv("TFA_DEBUG")) std::fprintf(stderr, "tfa_fwd: launch failed: %s\n", cudaGetErrorString(e));
-    return TFA_ERR_CUDA;
-  }
+  if (e != cudaSuccess) return fail(e);
   if (ev_end && cudaEventRecord(reinterpret_cast<cudaEvent_t>(ev_end), s) != cudaSuccess) return TFA_ERR_CUDA;
+  const int64_t G = a->num_q_heads / a->num_kv_heads;
+  if (fp.mixed && fp.dec.combine) {
+    const int64_t rows = std::min<int64_t>(fp.dec.rows, (16 / G) * G);
+    e = a->head_dim == 64 ? launch_combine<64>(pd, (int)rows, s) : launch_combine<128>(pd, (int)rows, s);
+    if (e != cudaSuccess) return fail(e);
+  }
   if (pl.combine) {
     // packed rows per group: at most one q tile, at most the longest query times the group
-    const int64_t rows = std::min<int64_t>(pl.rows, a->max_seqlen_q * (a->num_q_heads / a->num_kv_heads));
+    const int64_t rows = std::min<int64_t>(pl.rows, a->max_seqlen_q * G);
     e = a->head_dim == 64 ? launch_combine<64>(p, (int)rows, s) : launch_combine<128>(p, (int)rows, s);
-    if (e != cudaSuccess) return TFA_ERR_CUDA;
+    if (e != cudaSuccess) return fail(e);
   }
   return TFA_OK;
 }

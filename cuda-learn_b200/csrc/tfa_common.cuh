@@ -47,6 +47,8 @@ struct FwdParams {
   float* split_lse;        // [max_splits, total_q, Hq] fp32 (log2 domain, scaled)
   int* sched;              // [2]: next-item counter, finished-CTA counter (self-resetting)
   int* err;                // first device error code, 0 if none
+  int seq_filter;          // 0: every sequence; 1: only q_len * group <= 16 (decode-shaped);
+                           // 2: only q_len * group > 16 (a call split across both kernels)
 };
 
 // One unit of work: the packed q rows [row0, row0 + nrows) of kv head h of sequence b,
@@ -107,6 +109,8 @@ __device__ __forceinline__ Work get_work(const FwdParams& p, int idx) {
   w.kv_len = p.seqused_k[w.b];
   w.row0 = qt * p.rows_per_tile;
   w.nrows = imax(0, imin(p.rows_per_tile, w.q_len * p.group - w.row0));
+  // a sequence the other kernel of a mixed call handles has no rows here
+  if (p.seq_filter != 0 && ((p.seq_filter == 1) != (w.q_len * p.group <= 16))) w.nrows = 0;
   int t_lo, n;
   tile_span(p, w.q_len, w.kv_len, w.row0, w.nrows, t_lo, n);
   w.nsplits = splits_for(p, n);

@@ -89,7 +89,10 @@ typedef struct tfa_fwd_params {
 
 /* What tfa_fwd will launch for a given call (for tests, benches and tuning). */
 typedef struct tfa_plan_info {
-  int32_t kernel;         /* 0 = decode kernel (<= 16 packed q rows), 1 = prefill kernel */
+  int32_t kernel;         /* 0 = decode kernel (<= 16 packed q rows), 1 = prefill kernel, 2 = both: the
+                             decode kernel on sequences with q_len * group <= 16, the prefill kernel
+                             on the others (calls of >= 8 sequences that need the prefill kernel;
+                             the other fields then describe the prefill kernel's part) */
   int32_t rows_per_tile;  /* packed (q token, q head) rows per work item */
   int32_t q_tiles;        /* q tiles per (sequence, kv head) */
   int32_t max_splits;     /* split-KV slots per q tile */

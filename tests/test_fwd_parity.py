@@ -93,7 +93,7 @@ def test_two_tile_prefill_items(q_lens, hq, hkv, hd):
     c = case.to("cuda")
     p = faf.plan(c.q, c.k_cache, c.v_cache, c.cu_seqlens_q, c.seqused_k, c.block_table, c.max_seqlen_q,
                  c.max_seqlen_k, True)
-    assert p["kernel"] == 1 and p["rows_per_tile"] == 256
+    assert p["kernel"] in (1, 2) and p["rows_per_tile"] == 256  # 2: >= 8 sequences also run the decode kernel
     assert_parity(case)
 
 
@@ -262,3 +262,38 @@ def test_plan_decode_vs_prefill_selection():
     assert p["kernel"] == 1 and p["rows_per_tile"] in (128, 256)
     assert p["grid"] <= torch.cuda.get_device_properties(0).multi_processor_count
     assert math.isfinite(p["workspace_bytes"])
+
+
+# Mixed batches (vLLM chunked prefill: decode tokens and prompt chunks in one call) run
+# the decode kernel on decode-shaped sequences (q_len * group <= 16) and the prefill
+# kernel on the rest.
+MIXED = [
+    # q lens: decode tokens, short speculative chunks (q_len * G == 16 is still decode-shaped), prompt chunks
+    dict(q=[1, 1, 1, 4, 1, 2, 1, 40, 1, 300, 1, 3], k=[50, 700, 129, 260, 1, 33, 2048, 40, 900, 812, 16, 3],
+         heads=16, kv=4, d=128, causal=True, window=None),
+    dict(q=[1, 2, 1, 1, 17, 1, 1, 1, 1, 9], k=[300, 64, 1000, 5, 17, 128, 129, 2000, 77, 500],
+         heads=8, kv=1, d=64, causal=True, window=(100, 0)),
+    dict(q=[1] * 9 + [64], k=[33 * i + 1 for i in range(9)] + [200], heads=4, kv=4, d=64, causal=False,
+         window=None),
+]
+
+
+@pytest.mark.parametrize("cfg", MIXED, ids=["gqa4_d128", "gqa8_d64_window", "mha_d64_noncausal"])
+@pytest.mark.parametrize("splits", [0, 3])
+def test_mixed_batch_both_kernels(cfg, splits):
+    case = reference_case(cfg["q"], cfg["k"], num_heads=cfg["heads"], num_kv_heads=cfg["kv"], head_dim=cfg["d"],
+                          causal=cfg["causal"], window_size=cfg["window"], block_size=16, seed=21)
+    c = case.to("cuda")
+    p = faf.plan(c.q, c.k_cache, c.v_cache, c.cu_seqlens_q, c.seqused_k, c.block_table, c.max_seqlen_q,
+                 c.max_seqlen_k, c.causal, c.window_size, num_splits=splits)
+    assert p["kernel"] == 2
+    assert_parity(case, num_splits=splits)
+    # the same call again on the same workspace (control words left zeroed)
+    assert_parity(case, num_splits=splits)
+
+
+def test_mixed_batch_all_prefill_rows():
+    """A call that qualifies for both kernels but holds no decode-shaped sequence."""
+    case = reference_case([20] * 8, [20 + 7 * i for i in range(8)], num_heads=4, num_kv_heads=2, head_dim=64,
+                          causal=True, block_size=16, seed=22)
+    assert_parity(case)

@@ -191,3 +191,24 @@ def test_plan_small_decode_keeps_coarse_splits():
     info = _lib.TfaPlanInfo()
     assert _lib.load().tfa_plan(ctypes.byref(p), -1, ctypes.byref(info)) == 0
     assert info.kernel == 0 and info.split_cap == 5 and info.max_splits == 2
+
+
+@pytest.mark.parametrize("batch, heads, kv_heads, max_q, kernel", [
+    (8, 16, 4, 64, 2),    # prefill-shaped call with several sequences: both kernels
+    (4, 16, 4, 64, 1),    # few sequences: prefill kernel alone
+    (8, 34, 1, 64, 1),    # group > 16: no decode-shaped sequence can exist
+    (8, 16, 4, 4, 0),     # every sequence decode-shaped: decode kernel alone
+])
+def test_plan_mixed_dispatch(batch, heads, kv_heads, max_q, kernel):
+    p, _buf = _params(batch=batch, total_q=batch * max_q, num_q_heads=heads, num_kv_heads=kv_heads, head_dim=64,
+                      max_seqlen_q=max_q, max_seqlen_k=4096, causal=1)
+    p.q_stride[:] = [heads * 64, 64, 1]
+    p.out_stride[:] = [heads * 64, 64, 1]
+    p.k_stride[:] = [16 * kv_heads * 64, kv_heads * 64, 64, 1]
+    p.v_stride[:] = [16 * kv_heads * 64, kv_heads * 64, 64, 1]
+    p.num_blocks, p.block_table_stride0 = 4096, 256
+    lib = _lib.load()
+    info = _lib.TfaPlanInfo()
+    assert lib.tfa_plan(ctypes.byref(p), -1, ctypes.byref(info)) == 0
+    assert info.kernel == kernel
+    assert lib.tfa_workspace_size(ctypes.byref(p), -1) == info.workspace_bytes
