@@ -313,6 +313,10 @@ int fwd_impl(const tfa_fwd_params* a, void* workspace, size_t workspace_bytes, v
   const Plan& pl = fp.pre;
   FwdParams p;
   fill_params(a, pl, workspace, &p);
+  // Test hook for the kernels' time-limit path: with TFA_DEBUG_STALL_WAIT set, every CTA
+  // waits on a barrier that nothing arrives on until the wait's limit (1 s) expires; the
+  // call then reports error 102 through tfa_read_device_error. Nothing faults.
+  p.debug_stall = std::getenv("TFA_DEBUG_STALL_WAIT") ? 1 : 0;
   FwdParams pd;  // mixed calls: the decode kernel's part
   if (fp.mixed) {
     fill_params(a, fp.dec, reinterpret_cast<uint8_t*>(workspace) + fp.dec_off, &pd);
@@ -320,6 +324,7 @@ int fwd_impl(const tfa_fwd_params* a, void* workspace, size_t workspace_bytes, v
     // kernel's scheduler counters are its words 4-5, the error word is shared.
     pd.sched = p.sched + 4;
     pd.err = p.err;
+    pd.debug_stall = p.debug_stall;
     p.seq_filter = 2;
     pd.seq_filter = 1;
   }

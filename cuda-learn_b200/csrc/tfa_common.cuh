@@ -49,6 +49,7 @@ struct FwdParams {
   int* err;                // first device error code, 0 if none
   int seq_filter;          // 0: every sequence; 1: only q_len * group <= 16 (decode-shaped);
                            // 2: only q_len * group > 16 (a call split across both kernels)
+  int debug_stall;         // test hook: the MMA warp waits on a barrier nobody arrives on
 };
 
 // One unit of work: the packed q rows [row0, row0 + nrows) of kv head h of sequence b,

@@ -83,6 +83,7 @@ __global__ void __launch_bounds__(224, 1)
   __shared__ Work item_work[2];
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_flag;
+  __shared__ uint64_t stall_bar;  // never arrived on: the time-limit test hook waits here
   __shared__ __align__(16) float red_max[2][4][kNP];
   __shared__ __align__(16) float red_sum[2][4][kNP];
 
@@ -112,6 +113,7 @@ __global__ void __launch_bounds__(224, 1)
     }
     mbar_init(&red_bar, 4);
     abort_flag = 0;
+    mbar_init(&stall_bar, 1);
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -146,6 +148,9 @@ __global__ void __launch_bounds__(224, 1)
       const int idx = item_slot[slot];
       if (idx >= p.num_items) break;
       const Work w = item_work[slot];
+      // Test hook (FwdParams::debug_stall): wait for a phase that never completes, so the
+      // time limit expires, the error word is set and every warp of the CTA unwinds.
+      if (p.debug_stall && k == 0 && !mbar_wait(&stall_bar, 0, &abort_flag, p.err, kDevErrTimeoutMma)) break;
       const int n = w.tile_end - w.tile_begin;
       const uint32_t q_addr = smem_u32(q_smem + slot * Cfg::kQBytes);
       if (!mbar_wait(&q_full[slot], (k >> 1) & 1, &abort_flag, p.err, kDevErrTimeoutMma)) break;

@@ -69,6 +69,7 @@ __global__ void __launch_bounds__(320, 1)
   __shared__ int item_slot[2];
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_flag;
+  __shared__ uint64_t stall_bar;  // never arrived on: the time-limit test hook waits here
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -93,6 +94,7 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(&q_full[i], 8);
     }
     abort_flag = 0;
+    mbar_init(&stall_bar, 1);
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -149,6 +151,9 @@ __global__ void __launch_bounds__(320, 1)
       const int idx = item_slot[slot];
       if (idx >= p.num_items) break;
       const Work w = get_work(p, idx);
+      // Test hook (FwdParams::debug_stall): wait for a phase that never completes, so the
+      // time limit expires, the error word is set and every warp of the CTA unwinds.
+      if (p.debug_stall && k == 0 && !mbar_wait(&stall_bar, 0, &abort_flag, p.err, kDevErrTimeoutMma)) break;
       const int n = w.tile_end - w.tile_begin;
       const int nx = w.nrows > kRows ? 2 : 1;  // q tiles with rows
       if (!PROF_WAIT(3, mbar_wait(&q_full[slot], (k >> 1) & 1, &abort_flag, p.err, kDevErrTimeoutMma))) break;
