@@ -118,6 +118,16 @@ int make_plan_one(const tfa_fwd_params* p, int device, Plan* pl) {
     if (cap < 1) cap = 1;
     if (cap > 64) cap = 64;
     S = (tiles + cap - 1) / cap;
+    // Small decode calls are latency-bound: splits only help while all items still run in
+    // one wave of the grid; past that they add a wave and the combine.
+    const int64_t groups = (int64_t)p->batch * p->num_kv_heads * pl->q_tiles;
+    if (decode && est < 32 * (int64_t)sms && S > 1) {
+      const int64_t one_wave = groups > 0 ? sms / groups : S;
+      if (S > one_wave) {
+        S = one_wave < 1 ? 1 : one_wave;
+        cap = (tiles + S - 1) / S;
+      }
+    }
   }
   if (S < 1) S = 1;
   pl->max_splits = (int)S;
