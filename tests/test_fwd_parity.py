@@ -302,16 +302,18 @@ def test_mixed_batch_all_prefill_rows():
 @pytest.mark.parametrize("name", ["C2", "C1"], ids=["decode_split", "prefill"])
 def test_time_limit_reports_error_and_recovers(monkeypatch, name):
     """Every in-kernel wait is bounded. The test hook makes each CTA wait on a barrier
-    nothing arrives on: after the wait's limit (about 1 s) the call must record error 102
-    (time limit, MMA warp), every warp must unwind (no hang, no fault), the error word must
-    clear, and the next call on the same stream and workspace must be correct."""
+    nothing arrives on: after the wait's limit (about 1 s) the call must record a time-limit
+    error (101-103: whichever warp's wait expired first), every warp must unwind (no hang,
+    no fault), the error word must clear, and the next call on the same stream and workspace
+    must be correct."""
     case = baseline_config(name)
     c = case.to("cuda")
     out = torch.empty_like(c.q)
     monkeypatch.setenv("TFA_DEBUG_STALL_WAIT", "1")
     faf.flash_attn_varlen_func(**c.kwargs(), out=out)
     torch.cuda.synchronize()
-    assert faf.read_device_error() == 102
+    # the first limit to expire wins the error word: the MMA warp's (102) or a warp waiting on it (101, 103)
+    assert faf.read_device_error() in (101, 102, 103)
     assert faf.read_device_error() == 0
     monkeypatch.delenv("TFA_DEBUG_STALL_WAIT")
     assert_parity(case)
