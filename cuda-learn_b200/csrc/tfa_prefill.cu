@@ -48,11 +48,19 @@ struct PrefillCfg {
   static constexpr int kQBytes = kPanels * kRows * 128;        // per q tile
   static constexpr int kQOff = kSlots * kSlotBytes;
   static constexpr int kDynBytes = kQOff + 2 * kQBytes + 1024;
-  static constexpr uint32_t kTmemCols = 512;                   // S_A, S_B (P aliases their first 64), O_A, O_B
+  static constexpr uint32_t kTmemCols = 512;                   // S_A, S_B, O_A, O_B (+ P_A, P_B at D = 64)
+  // D = 64 leaves TMEM room for P of its own (O needs 64 columns per tile): QK(j+1) may then
+  // overwrite S as soon as the softmax has loaded S(j), overlapping the softmax's exponent
+  // phase. At D = 128 (2 x 128 S + 2 x 128 O = 512 columns) P aliases the first 64 S columns.
+  static constexpr bool kSeparateP = (D == 64);
 };
 
 __device__ __forceinline__ uint32_t s_col_of(int x) { return x == 0 ? 0u : 128u; }
 __device__ __forceinline__ uint32_t o_col_of(int x) { return x == 0 ? 256u : 384u; }
+template <int D>
+__device__ __forceinline__ uint32_t p_col_of(int x) {
+  return D == 64 ? (x == 0 ? 320u : 448u) : s_col_of(x);  // D = 64: after O's 64 columns
+}
 
 template <int D>
 __global__ void __launch_bounds__(320, 1)
@@ -64,7 +72,7 @@ __global__ void __launch_bounds__(320, 1)
   uint8_t* q_smem = smem + Cfg::kQOff;
 
   __shared__ uint64_t full[Cfg::kSlots], empty[Cfg::kSlots];
-  __shared__ uint64_t s_full[2], p_full[2], o_full[2], o_free[2];
+  __shared__ uint64_t s_full[2], s_free[2], p_full[2], o_full[2], o_free[2];
   __shared__ uint64_t item_full[2], item_empty[2], q_full[2];
   __shared__ int item_slot[2];
   __shared__ uint32_t tmem_base_sh;
@@ -86,6 +94,7 @@ __global__ void __launch_bounds__(320, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 4);  // D = 64: the softmax warpgroup has loaded S
       mbar_init(&p_full[i], 4);
       mbar_init(&o_full[i], 1);
       mbar_init(&o_free[i], 4);
@@ -136,7 +145,7 @@ __global__ void __launch_bounds__(320, 1)
     };
     auto issue_pv = [&](int x, int vslot, bool first) {
       const uint32_t v_addr = smem_u32(slots + vslot * Cfg::kSlotBytes);
-      const uint32_t p_tmem = tmem + s_col_of(x);  // P (bf16 pairs) over the first 64 S columns
+      const uint32_t p_tmem = tmem + p_col_of<D>(x);  // P as bf16 pairs (over S's first 64 columns at D = 128)
 #pragma unroll
       for (int kk = 0; kk < kBN / 16; ++kk) {
         umma_bf16_ts(tmem + o_col_of(x), p_tmem + kk * 8,
@@ -168,6 +177,43 @@ __global__ void __launch_bounds__(320, 1)
         for (int j = 0; ok && j < n; ++j) {
           const int kc = c + 2 * j;  // slot load index of K_j; V_j is kc + 1
           const bool more = j + 1 < n;
+          if constexpr (Cfg::kSeparateP) {
+            // QK(j+1) as soon as the softmax has loaded S(j) (P lives elsewhere), then P.V(j)
+            if (more) {
+              if (!slot_wait(kc + 2)) {  // K_{j+1}
+                ok = false;
+                break;
+              }
+              for (int x = 0; x < nx; ++x) {
+                if (!PROF_WAIT(2, mbar_wait(&s_free[x], (x ? ts1 : ts0) & 1, &abort_flag, p.err, kDevErrTimeoutMma))) {
+                  ok = false;
+                  break;
+                }
+                tc_fence_after();
+                issue_qk(x, (kc + 2) % Cfg::kSlots);
+              }
+              if (!ok) break;
+              umma_commit(&empty[(kc + 2) % Cfg::kSlots]);  // K_{j+1} consumed
+            }
+            if (!slot_wait(kc + 1)) {  // V_j
+              ok = false;
+              break;
+            }
+            for (int x = 0; x < nx; ++x) {
+              const int tsx = x ? ts1 : ts0, oix = x ? oi1 : oi0;
+              if (!PROF_WAIT(1, mbar_wait(&p_full[x], tsx & 1, &abort_flag, p.err, kDevErrTimeoutMma)) ||
+                  (j == 0 && !PROF_WAIT(2, mbar_wait(&o_free[x], (oix & 1) ^ 1, &abort_flag, p.err, kDevErrTimeoutMma)))) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              issue_pv(x, (kc + 1) % Cfg::kSlots, j == 0);
+              if (x) ++ts1; else ++ts0;
+            }
+            if (!ok) break;
+            umma_commit(&empty[(kc + 1) % Cfg::kSlots]);  // V_j consumed
+            continue;
+          }
           if (!slot_wait(kc + 1)) {  // V_j
             ok = false;
             break;
@@ -219,6 +265,7 @@ __global__ void __launch_bounds__(320, 1)
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
     const uint32_t s_col = lane_base + s_col_of(x);
     const uint32_t o_col = lane_base + o_col_of(x);
+    const uint32_t p_col = lane_base + p_col_of<D>(x);
     uint8_t* q_tile = q_smem + x * Cfg::kQBytes;
     int ts = 0;  // kv tiles processed by this q tile (phase counter)
     for (int k = 0;; ++k) {
@@ -270,6 +317,11 @@ __global__ void __launch_bounds__(320, 1)
         // the whole 128-score row in registers, one TMEM load
         float sv[128];
         tmem_ld128_sync(s_col, sv);
+        if constexpr (Cfg::kSeparateP) {  // S(j) is in registers: QK(j+1) may overwrite it
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s_free[x]);
+        }
         // row max over 8 independent partial maxima, three-input max (short chains)
         float m8[8];
 #pragma unroll
@@ -292,10 +344,14 @@ __global__ void __launch_bounds__(320, 1)
           }
           m_ref = tmax;
         }
-        // Rescaling O needs the previous P.V of this q tile complete. Writing P needs no
-        // wait: P(j) overwrites only S(j), and the MMA warp issued QK(j) after P.V(j-1),
-        // which read P(j-1) from those columns, had completed.
-        if (j > 0 && __any_sync(0xffffffffu, rescale)) {
+        // Rescaling O needs the previous P.V of this q tile complete. At D = 128 writing P
+        // needs no wait: P(j) overwrites only S(j), and the MMA warp issued QK(j) after
+        // P.V(j-1), which read P(j-1) from those columns, had completed. At D = 64 P has
+        // columns of its own, which P.V(j-1) reads: that wait comes just before the first
+        // P store, so the exponentials overlap it.
+        const bool rescale_any = j > 0 && __any_sync(0xffffffffu, rescale);
+        bool p_wait = Cfg::kSeparateP && j > 0 && !rescale_any;
+        if (rescale_any) {
           if (!PROF_WAIT(1, mbar_wait(&o_full[x], (ts - 1) & 1, &abort_flag, p.err, kDevErrTimeoutSoftmax))) {
             ok = false;
             break;
@@ -315,7 +371,7 @@ __global__ void __launch_bounds__(320, 1)
           }
         }
         l *= alpha;
-        // P = 2^(s*scale - m_ref) -> bf16 pairs -> TMEM (over the S columns), row sum
+        // P = 2^(s*scale - m_ref) -> bf16 pairs -> TMEM (P's columns), row sum
         const float ms = (m_ref == -INFINITY) ? 0.f : m_ref;
         const uint64_t scale2 = f2_pack(p.scale_log2, p.scale_log2);
         const uint64_t neg_ms2 = f2_pack(-ms, -ms);
@@ -333,9 +389,15 @@ __global__ void __launch_bounds__(320, 1)
             __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
             pk[c] = __uint_as_float(*reinterpret_cast<uint32_t*>(&h2));
           }
-          tmem_st32(s_col + h * 32, pk);
+          if (h == 0 && p_wait) {
+            if (!mbar_wait(&o_full[x], (ts - 1) & 1, &abort_flag, p.err, kDevErrTimeoutSoftmax)) ok = false;
+            tc_fence_after();
+            p_wait = false;
+          }
+          tmem_st32(p_col + h * 32, pk);
         }
         tmem_wait_st();
+        if (!ok) break;
         float r0, r1, r2, r3;
         f2_unpack(rs2[0], r0, r1);
         f2_unpack(rs2[1], r2, r3);
