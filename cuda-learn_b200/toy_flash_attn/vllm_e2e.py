@@ -80,7 +80,7 @@ def _reinit(std: float):
     return fn
 
 
-def run(backend: str, num_prompts: int, max_tokens: int, std: float) -> dict:
+def run(backend: str, num_prompts: int, max_tokens: int, std: float, max_batched_tokens: int | None = None) -> dict:
     os.environ.setdefault("VLLM_ENABLE_V1_MULTIPROCESSING", "0")  # keep the engine in this process
     os.environ.setdefault("HF_HUB_OFFLINE", "1")
     os.environ.setdefault("TRANSFORMERS_OFFLINE", "1")
@@ -102,9 +102,13 @@ def run(backend: str, num_prompts: int, max_tokens: int, std: float) -> dict:
     with tempfile.TemporaryDirectory() as d:
         (Path(d) / "config.json").write_text(json.dumps(QWEN2_SMALL))
         t0 = time.time()
+        extra = {}
+        if max_batched_tokens:  # small budgets make chunked prefill mix prompt chunks with decodes
+            extra = dict(max_num_batched_tokens=max_batched_tokens, enable_chunked_prefill=True)
         llm = LLM(model=d, skip_tokenizer_init=True, load_format="dummy", dtype="bfloat16", seed=0,
                   max_model_len=2048, gpu_memory_utilization=0.5, max_num_seqs=num_prompts, enforce_eager=True,
-                  attention_backend=backend, kv_cache_dtype="bfloat16" if backend == "CUSTOM" else "auto")
+                  attention_backend=backend, kv_cache_dtype="bfloat16" if backend == "CUSTOM" else "auto",
+                  **extra)
         t_init = time.time() - t0
         if std > 0:
             llm.apply_model(_reinit(std))
@@ -147,13 +151,15 @@ def main() -> None:
     ap.add_argument("--max-tokens", type=int, default=64)
     ap.add_argument("--out", default=None)
     ap.add_argument("--std", type=float, default=0.02, help="redraw weights from N(0, std); 0 keeps vLLM's dummy init")
+    ap.add_argument("--max-batched-tokens", type=int, default=None,
+                    help="vLLM max_num_batched_tokens (small values mix prompt chunks with decode steps)")
     ap.add_argument("--compare", nargs=2, default=None, help="two result files to compare instead of running")
     args = ap.parse_args()
     if args.compare:
         a, b = (json.loads(Path(f).read_text()) for f in args.compare)
         res = compare(a, b)
     else:
-        res = run(args.backend, args.num_prompts, args.max_tokens, args.std)
+        res = run(args.backend, args.num_prompts, args.max_tokens, args.std, args.max_batched_tokens)
     text = json.dumps(res)
     print(text)
     if args.out:
