@@ -136,17 +136,19 @@ __device__ __forceinline__ void scheduler_finish(const FwdParams& p) {
 }
 
 // ---------------------------------------------------------------------------
-// Paged K/V producer: one warp gathers the 128-token tile of kv head h of sequence b
-// into a pipeline stage laid out as [V panels][K panels], each panel 128 rows x 128 B
-// (64 head-dim columns, 128-byte swizzle). Rows at or past kv_len are zero-filled by
-// out-of-range TMA coordinates, so stale or NaN cache slots never reach an MMA.
+// Paged K/V gather: a producer warp fetches the 128-token tile of kv head h of sequence b
+// page group by page group (one TMA box per 16-slot group and 64 columns). One tile of one
+// tensor is kPanels panels of 128 rows x 128 B (64 head-dim columns, 128-byte swizzle);
+// the gather debug kernel stages V and K of a tile together as [V panels][K panels]. Rows
+// at or past kv_len are zero-filled by out-of-range TMA coordinates, so stale or NaN cache
+// slots never reach an MMA.
 // ---------------------------------------------------------------------------
 template <int D>
 struct KvStage {
   static constexpr int kPanels = D / 64;
   static constexpr int kPanelBytes = kBN * 128;            // 16 KB
   static constexpr int kTensorBytes = kPanels * kPanelBytes;
-  static constexpr int kBytes = 2 * kTensorBytes;          // V then K
+  static constexpr int kBytes = 2 * kTensorBytes;          // V then K (gather debug kernel)
 };
 
 struct KvMaps {
@@ -276,8 +278,9 @@ __device__ void decode_stamp_hook(int i);
 
 // Producer warp main loop of the decode kernel. Fetches work items dynamically,
 // publishes each (index, descriptor, and its Q rows loaded by TMA) into the two-slot item
-// queue and streams their kv tiles, so the consumers start an item without global loads. When a tile
-// has at most 32 groups (block_size >= 4), lane g owns group g and the block-table
+// queue, so the consumers start an item without global loads, and streams the K tiles of
+// its items into the K ring. When a tile has at most 32 groups (block_size >= 4), lane g
+// owns group g and the block-table
 // entries of tile t+1 are requested before the wait for tile t's free stage, so the
 // table latency hides behind the pipeline; the next item is claimed while the last tile
 // of the current one waits for its stage. The first item of CTA i is item i; later items
