@@ -280,10 +280,9 @@ __device__ void decode_stamp_hook(int i);
 // publishes each (index, descriptor, and its Q rows loaded by TMA) into the two-slot item
 // queue, so the consumers start an item without global loads, and streams the K tiles of
 // its items into the K ring. When a tile has at most 32 groups (block_size >= 4), lane g
-// owns group g and the block-table
-// entries of tile t+1 are requested before the wait for tile t's free stage, so the
-// table latency hides behind the pipeline; the next item is claimed while the last tile
-// of the current one waits for its stage. The first item of CTA i is item i; later items
+// owns group g and the block-table entries of tile t+1 are requested before the wait for
+// tile t's free slot, so the table latency hides behind the pipeline; the next item is
+// claimed while the last tile of the current one waits for its slot. The first item of CTA i is item i; later items
 // come from the shared counter offset by the grid size, so start-up has no atomic.
 template <int D, int STAGES>
 __device__ __forceinline__ void producer_loop(const FwdParams& p, const KvMaps& maps, uint8_t* ring,

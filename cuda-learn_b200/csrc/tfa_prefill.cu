@@ -14,11 +14,13 @@
 //   S[128 x 128] = Q[128 x D] . K^T   (tcgen05, A = Q K-major, B = K K-major), S in TMEM
 //   O[128 x D]  += P[128 x 128] . V   (tcgen05, A = P from TMEM, B = V MN-major), O in TMEM
 // Softmax threads own one row each (TMEM lane = row) and hold its 128 scores in
-// registers (one TMEM load per tile); P is stored back as bf16 pairs over the first 64
-// columns of the same S region and read from there by the P.V MMA, so P never touches
-// shared memory (whose bandwidth the MMAs' smem operands and the TMA fills already use). O is rescaled in TMEM only when a row's max grows by more than 2^8 over the max
-// its P values are referenced to (values of P stay <= 256, far inside bf16/fp32 range),
-// so most tiles need no O round trip.
+// registers (one TMEM load per tile); P is stored back to TMEM as bf16 pairs and read from
+// there by the P.V MMA, so P never touches shared memory (whose bandwidth the MMAs' smem
+// operands and the TMA fills already use). At D = 128 P overwrites the first 64 columns of
+// the tile's S region; at D = 64 it has columns of its own, so the next QK may start as
+// soon as S has been loaded. O is rescaled in TMEM only when a row's max grows by more
+// than 2^8 over the max its P values are referenced to (values of P stay <= 256, far inside
+// bf16/fp32 range), so most tiles need no O round trip.
 //
 // Warps (320 threads): 0 = TMA producer (K and V in separate slots), 1 = MMA issuer and
 // TMEM owner, 2-5 = softmax/epilogue of tile A, 6-9 = softmax/epilogue of tile B.
