@@ -275,14 +275,21 @@ MIXED = [
          heads=8, kv=1, d=64, causal=True, window=(100, 0)),
     dict(q=[1] * 9 + [64], k=[33 * i + 1 for i in range(9)] + [200], heads=4, kv=4, d=64, causal=False,
          window=None),
+    # group 16: one q token is exactly 16 rows (decode-shaped), two are prefill-shaped
+    dict(q=[1, 2, 1, 1, 1, 1, 1, 3], k=[100, 300, 17, 2049, 64, 65, 1, 500], heads=32, kv=2, d=128, causal=True,
+         window=None),
+    # two-sided window, not causal
+    dict(q=[1, 1, 30, 1, 1, 1, 1, 5], k=[400, 90, 260, 33, 1000, 128, 7, 77], heads=8, kv=2, d=64, causal=False,
+         window=(48, 16)),
 ]
 
 
-@pytest.mark.parametrize("cfg", MIXED, ids=["gqa4_d128", "gqa8_d64_window", "mha_d64_noncausal"])
+@pytest.mark.parametrize("cfg", MIXED, ids=["gqa4_d128", "gqa8_d64_window", "mha_d64_noncausal", "gqa16_d128",
+                                         "two_sided_window"])
 @pytest.mark.parametrize("splits", [0, 3])
 def test_mixed_batch_both_kernels(cfg, splits):
     case = reference_case(cfg["q"], cfg["k"], num_heads=cfg["heads"], num_kv_heads=cfg["kv"], head_dim=cfg["d"],
-                          causal=cfg["causal"], window_size=cfg["window"], block_size=16, seed=21)
+                          causal=cfg["causal"], window_size=cfg["window"], block_size=cfg.get("bs", 16), seed=21)
     c = case.to("cuda")
     p = faf.plan(c.q, c.k_cache, c.v_cache, c.cu_seqlens_q, c.seqused_k, c.block_table, c.max_seqlen_q,
                  c.max_seqlen_k, c.causal, c.window_size, num_splits=splits)
@@ -317,3 +324,11 @@ def test_time_limit_reports_error_and_recovers(monkeypatch, name):
     assert faf.read_device_error() == 0
     monkeypatch.delenv("TFA_DEBUG_STALL_WAIT")
     assert_parity(case)
+
+
+def test_mixed_batch_large_pages():
+    """Mixed dispatch with 64-token pages (one page covers half a kv tile)."""
+    case = reference_case([1, 1, 1, 1, 40, 1, 1, 2], [500, 64, 65, 1, 300, 129, 700, 90], num_heads=8,
+                          num_kv_heads=2, head_dim=128, causal=True, block_size=64, seed=23)
+    assert_parity(case)
+
