@@ -332,3 +332,22 @@ def test_mixed_batch_large_pages():
                           num_kv_heads=2, head_dim=128, causal=True, block_size=64, seed=23)
     assert_parity(case)
 
+
+
+@pytest.mark.parametrize("bs", [1, 4])
+def test_mixed_batch_small_pages_and_empty_sequences(bs):
+    """Mixed dispatch with empty queries, empty caches and sub-16-token pages."""
+    case = reference_case([1, 0, 1, 12, 1, 1, 0, 2], [50, 30, 0, 70, 129, 1, 0, 19], num_heads=8, num_kv_heads=2,
+                          head_dim=64, causal=True, block_size=bs, seed=24)
+    out, _ = run_cuda(case)
+    ref, _ = oracle(case)
+    # rows of a sequence with an empty cache attend to nothing: the reference's softmax of an
+    # all-masked row is NaN, this library writes zeros (and -inf LSE); compare the others
+    q0 = case.cu_seqlens_q.tolist()
+    keep = torch.ones(out.shape[0], dtype=torch.bool)
+    for b, kv in enumerate(case.seqused_k.tolist()):
+        if kv == 0:
+            keep[q0[b]:q0[b + 1]] = False
+    assert torch.isfinite(out.float()).all()
+    assert (out.float()[keep] - ref[keep]).abs().max().item() <= OUT_TOL
+    assert torch.all(out[~keep] == 0)
