@@ -424,7 +424,12 @@ def run_ours(args):
     kvb_total = kvb_local * world
     out = torch.empty_like(case.q)
     p = plan_of(case)
-    launches_per_step = 1 + p["combine"]
+    # the attention kernel, the split combine, and the item-list kernel where the library
+    # builds one (decode with splits, > 2 slots per SM, < 1024 tiles per SM of the length bound)
+    tiles_bound = case.batch * case.k_cache.shape[2] * ((case.max_seqlen_k + 127) // 128)
+    list_kernel = int(p["kernel"] == 0 and p["max_splits"] > 1 and p["num_items"] > 2 * p["grid"]
+                      and tiles_bound < 1024 * p["grid"])
+    launches_per_step = 1 + p["combine"] + list_kernel
 
     for _ in range(max(args.warmup, 3)):
         call(case, out)

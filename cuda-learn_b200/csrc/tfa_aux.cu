@@ -88,6 +88,47 @@ __global__ void __launch_bounds__(512) combine_kernel(const __grid_constant__ Fw
   }
 }
 
+// Builds the decode kernel's item list for one call: every existing (group, split) item,
+// ordered by kv tiles per split, longest first, so the persistent grid hands out the long
+// items early and the short ones (whole short sequences) last, which shortens its tail.
+// One CTA; a counting sort over the tiles-per-split key (splits hold at most 64 tiles).
+// Entry = g * max_splits + split; the number of entries goes to *count.
+__global__ void __launch_bounds__(1024) item_list_kernel(const __grid_constant__ FwdParams p, int* list, int* count) {
+  constexpr int kKeys = 65;
+  __shared__ int hist[kKeys];
+  __shared__ int base[kKeys];
+  const int groups = p.q_tiles * p.batch * p.hkv;
+  for (int i = threadIdx.x; i < kKeys; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  auto key_of = [&](int g, int& ns) {
+    const Work w = work_of(p, g, 0);
+    ns = w.exists ? w.nsplits : 0;
+    return kKeys - 1 - imin(kKeys - 1, w.tile_end - w.tile_begin);
+  };
+  for (int g = threadIdx.x; g < groups; g += blockDim.x) {
+    int ns;
+    const int key = key_of(g, ns);
+    if (ns) atomicAdd(&hist[key], ns);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int i = 0; i < kKeys; ++i) {
+      base[i] = acc;
+      acc += hist[i];
+    }
+    *count = acc;
+  }
+  __syncthreads();
+  for (int g = threadIdx.x; g < groups; g += blockDim.x) {
+    int ns;
+    const int key = key_of(g, ns);
+    if (!ns) continue;
+    const int pos = atomicAdd(&base[key], ns);
+    for (int sp = 0; sp < ns; ++sp) list[pos + sp] = g * p.max_splits + sp;
+  }
+}
+
 // One CTA per (kv tile, sequence, kv head): the producer warp stages the tile with the
 // attention kernels' TMA gather (produce_tile), then all threads copy the valid rows out.
 template <int D>
@@ -160,6 +201,11 @@ cudaError_t launch_gather(const FwdParams& p, const KvMaps& maps, int max_tiles,
   dim3 grid(max_tiles, p.batch, p.hkv);
   gather_kernel<D><<<grid, 128, smem, s>>>(p, maps, kv_offsets, reinterpret_cast<__nv_bfloat16*>(k_out),
                                            reinterpret_cast<__nv_bfloat16*>(v_out));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_item_list(const FwdParams& p, int* list, int* count, cudaStream_t s) {
+  item_list_kernel<<<1, 1024, 0, s>>>(p, list, count);
   return cudaGetLastError();
 }
 

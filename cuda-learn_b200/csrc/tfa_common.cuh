@@ -50,6 +50,9 @@ struct FwdParams {
   int seq_filter;          // 0: every sequence; 1: only q_len * group <= 16 (decode-shaped);
                            // 2: only q_len * group > 16 (a call split across both kernels)
   int debug_stall;         // test hook: the MMA warp waits on a barrier nobody arrives on
+  const int* item_list;    // decode kernel: existing items (g * max_splits + split), longest
+                           // first, built on the device for the call (NULL: slot order)
+  const int* item_count;   // number of entries of item_list
 };
 
 // One unit of work: the packed q rows [row0, row0 + nrows) of kv head h of sequence b,
@@ -120,6 +123,20 @@ __device__ __forceinline__ Work get_work(const FwdParams& p, int idx) {
   w.tile_end = t_lo + (int)(((long long)n * (w.split + 1)) / w.nsplits);
   if (!w.exists) w.tile_end = w.tile_begin;
   return w;
+}
+
+// Work item of group g (= q tile slot, sequence, kv head: the get_work order with
+// split 0) and split slot `split`.
+__device__ __forceinline__ Work work_of(const FwdParams& p, int g, int split) {
+  const int groups = p.q_tiles * p.batch * p.hkv;
+  return get_work(p, split * groups + g);
+}
+
+// Item idx of the device-built list (only compiled into the decode kernel instance that
+// runs with a list, so no load through the list pointer exists where it is null).
+__device__ __forceinline__ Work get_work_from_list(const FwdParams& p, int idx) {
+  const int e = p.item_list[idx];
+  return work_of(p, e / p.max_splits, e % p.max_splits);
 }
 
 // Called once per CTA by the producer's lane 0 after its final (out-of-range) claim: no
@@ -284,7 +301,7 @@ __device__ void decode_stamp_hook(int i);
 // tile t's free slot, so the table latency hides behind the pipeline; the next item is
 // claimed while the last tile of the current one waits for its slot. The first item of CTA i is item i; later items
 // come from the shared counter offset by the grid size, so start-up has no atomic.
-template <int D, int STAGES>
+template <int D, int STAGES, bool kList>
 __device__ __forceinline__ void producer_loop(const FwdParams& p, const KvMaps& maps, uint8_t* ring,
                                               uint64_t* full, uint64_t* empty, uint64_t* item_full,
                                               uint64_t* item_empty, int* item_slot, Work* item_work,
@@ -296,6 +313,9 @@ __device__ __forceinline__ void producer_loop(const FwdParams& p, const KvMaps& 
   const int q_tokens = 16 / p.group;  // tokens per Q box (G heads each)
   const uint32_t q_tx = (uint32_t)(KvStage<D>::kPanels * p.group * q_tokens * 128);
   int c = 0;
+  // item indices handed out: the device-built list's length, or every slot
+  int bound = p.num_items;
+  if constexpr (kList) bound = *reinterpret_cast<const volatile int*>(p.item_count);
   int claimed = (lane == 0) ? (int)blockIdx.x : 0;  // next item index (lane 0)
   auto claim = [&]() {
     if (lane == 0) claimed = atomicAdd(&p.sched[0], 1) + (int)gridDim.x;
@@ -306,15 +326,16 @@ __device__ __forceinline__ void producer_loop(const FwdParams& p, const KvMaps& 
     int idx = __shfl_sync(0xffffffffu, claimed, 0);
     Work w;
     // Skip split slots a sequence does not use without bothering the consumers.
-    while (idx < p.num_items) {
-      w = get_work(p, idx);
+    while (idx < bound) {
+      if constexpr (kList) w = get_work_from_list(p, idx);
+      else w = get_work(p, idx);
       if (w.exists) break;
       claim();
       idx = __shfl_sync(0xffffffffu, claimed, 0);
     }
     if (lane == 0) {
-      item_slot[slot] = idx;
-      if (idx < p.num_items) {
+      item_slot[slot] = idx < bound ? idx : p.num_items;  // the consumers stop at num_items
+      if (idx < bound) {
         // The item's descriptor and Q rows (all heads of the group, its tokens, packed-row
         // order) go into this slot's buffers. The slot's previous item has finished: its
         // consumers arrived on item_empty only after its last MMA completed.
@@ -327,7 +348,7 @@ __device__ __forceinline__ void producer_loop(const FwdParams& p, const KvMaps& 
       }
       mbar_arrive(&item_full[slot]);
     }
-    if (idx >= p.num_items) {
+    if (idx >= bound) {
       if (lane == 0) scheduler_finish(p);
       return;
     }
@@ -516,6 +537,7 @@ template <int D>
 cudaError_t launch_prefill(const FwdParams& p, const KvMaps& maps, int grid, cudaStream_t s);
 template <int D>
 cudaError_t launch_combine(const FwdParams& p, int max_rows, cudaStream_t s);
+cudaError_t launch_item_list(const FwdParams& p, int* list, int* count, cudaStream_t s);
 template <int D>
 cudaError_t launch_gather(const FwdParams& p, const KvMaps& maps, int max_tiles, const int64_t* kv_offsets,
                           void* k_out, void* v_out, cudaStream_t s);

@@ -64,7 +64,7 @@ struct DecodeCfg {
   static constexpr uint32_t kTmemCols = 64;              // S^T x2 (16 cols), O^T x2 (16 cols)
 };
 
-template <int D>
+template <int D, bool kList>
 __global__ void __launch_bounds__(224, 1)
     decode_kernel(const __grid_constant__ FwdParams p, const __grid_constant__ KvMaps maps,
                   const __grid_constant__ CUtensorMap q_map) {
@@ -131,7 +131,7 @@ __global__ void __launch_bounds__(224, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    producer_loop<D, Cfg::kKSlots>(p, maps, k_ring, full_k, empty_k, item_full, item_empty, item_slot, item_work, &q_map,
+    producer_loop<D, Cfg::kKSlots, kList>(p, maps, k_ring, full_k, empty_k, item_full, item_empty, item_slot, item_work, &q_map,
                                    q_smem, Cfg::kQBytes, q_full, &abort_flag, lane);
   } else if (warp == 6) {
     producer_follow_v<D, Cfg::kVSlots>(p, maps, v_ring, full_v, empty_v, item_full, item_empty, item_slot, item_work,
@@ -469,17 +469,21 @@ int decode_smem_bytes() {
 
 template <int D>
 cudaError_t launch_decode(const FwdParams& p, const KvMaps& maps, const CUtensorMap& q_map, int grid, cudaStream_t s) {
-  static bool configured[128] = {};
+  static bool configured[128][2] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
-  if (!configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(decode_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         DecodeCfg<D>::kDynBytes);
+  const int li = p.item_list != nullptr ? 1 : 0;  // the instance that reads the item list
+  if (!configured[dev][li]) {
+    cudaError_t e = cudaFuncSetAttribute(li ? decode_kernel<D, true> : decode_kernel<D, false>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, DecodeCfg<D>::kDynBytes);
     if (e != cudaSuccess) return e;
-    configured[dev] = true;
+    configured[dev][li] = true;
   }
-  decode_kernel<D><<<grid, 224, DecodeCfg<D>::kDynBytes, s>>>(p, maps, q_map);
+  if (li)
+    decode_kernel<D, true><<<grid, 224, DecodeCfg<D>::kDynBytes, s>>>(p, maps, q_map);
+  else
+    decode_kernel<D, false><<<grid, 224, DecodeCfg<D>::kDynBytes, s>>>(p, maps, q_map);
   return cudaGetLastError();
 }
 

@@ -351,3 +351,20 @@ def test_mixed_batch_small_pages_and_empty_sequences(bs):
     assert torch.isfinite(out.float()).all()
     assert (out.float()[keep] - ref[keep]).abs().max().item() <= OUT_TOL
     assert torch.all(out[~keep] == 0)
+
+
+def test_decode_with_device_item_list():
+    """A decode call with split slots to spare and a small work bound takes its items from a
+    list built on the device, longest first; results must not depend on that order."""
+    g = torch.Generator().manual_seed(31)
+    k_lens = [int(x) for x in torch.exp(torch.empty(64).uniform_(0, math.log(8192), generator=g)).round().clamp(1, 8192)]
+    k_lens[0] = 8192
+    case = reference_case([1] * 64, k_lens, num_heads=16, num_kv_heads=4, head_dim=128, causal=True, block_size=16,
+                          seed=31)
+    c = case.to("cuda")
+    p = faf.plan(c.q, c.k_cache, c.v_cache, c.cu_seqlens_q, c.seqused_k, c.block_table, c.max_seqlen_q,
+                 c.max_seqlen_k, True)
+    assert p["kernel"] == 0 and p["max_splits"] > 1 and p["num_items"] > 2 * p["grid"]
+    out, _ = assert_parity(case)
+    out2, _ = run_cuda(case)
+    assert torch.equal(out, out2)
