@@ -63,6 +63,11 @@ __device__ __forceinline__ float lg2_approx(float x) {
   return y;
 }
 
+// Brings the 128-byte line holding `p` into L2 (no register result, nothing waits on it).
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(p)));
+}
+
 // Named barrier over a subset of the CTA's warps (id 0 is __syncthreads).
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");

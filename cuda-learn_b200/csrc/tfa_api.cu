@@ -16,6 +16,12 @@ namespace tfa {
 namespace {
 
 constexpr size_t kCtrlBytes = 256;  // workspace control block: sched[2], err, decode sched[2] at 4-5, item count at 6
+// Calls with split-KV reserve a fixed region after the control block for the decode
+// kernel's per-group split counters. It sits at the same place for every call shape and
+// nothing else is ever written there, so, like the control block, it only has to be
+// zeroed when the workspace is allocated (each call leaves its counters at zero).
+constexpr size_t kCounterRegionEnd = 64 * 1024;
+constexpr int64_t kMaxCountedGroups = (int64_t)((kCounterRegionEnd - kCtrlBytes) / sizeof(int));
 constexpr int kMaxDevices = 128;
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -66,9 +72,13 @@ int validate(const tfa_fwd_params* p) {
 
 struct Plan {
   int kernel;
-  int rows, q_tiles, max_splits, split_cap, num_items, grid, combine;
+  int rows, q_tiles, max_splits, split_cap, num_items, grid;
+  int combine;         // 0: no splits; 1: the combine kernel merges them; 2: the decode kernel does
   int item_list;       // decode with splits and many slots: a device-built, longest-first item list
-  size_t list_off;     // its byte offset in the workspace
+  size_t cnt_off;      // byte offset of the per-group split counters (combine == 2)
+  size_t lse_off, o_off;  // byte offsets of the split partials
+  size_t list_off;     // byte offset of the item list
+  size_t zero_bytes;   // leading bytes that must be zero before a call (control block, counters)
   size_t ws_bytes;
 };
 
@@ -140,11 +150,24 @@ int make_plan_one(const tfa_fwd_params* p, int device, Plan* pl) {
   pl->num_items = (int)items;
   pl->grid = (int)(items < sms ? items : sms);
   if (pl->grid < 1) pl->grid = 1;
-  pl->combine = S > 1 ? 1 : 0;
+  // Split partials are merged by the decode kernel itself (the last split of a group to
+  // finish, counted per group in the reserved counter region) or, after the prefill
+  // kernel and for decode calls with more groups than the region counts, by the combine
+  // kernel.
+  const int64_t groups = (int64_t)p->batch * p->num_kv_heads * pl->q_tiles;
+  pl->combine = S > 1 ? ((decode && groups <= kMaxCountedGroups) ? 2 : 1) : 0;
   size_t ws = kCtrlBytes;
+  pl->cnt_off = pl->lse_off = pl->o_off = 0;
+  if (S > 1) {
+    pl->cnt_off = kCtrlBytes;
+    ws = kCounterRegionEnd;
+  }
+  pl->zero_bytes = ws;
   if (S > 1) {
     const size_t rows = (size_t)S * p->total_q * p->num_q_heads;
+    pl->lse_off = ws;
     ws += align_up(rows * sizeof(float), 256);
+    pl->o_off = ws;
     ws += rows * p->head_dim * sizeof(float);
   }
   // Decode calls with split slots to spare may take their items from a list built on the
@@ -177,6 +200,9 @@ struct FullPlan {
   int mixed;
   size_t dec_off;  // mixed: byte offset of the decode part of the workspace
   size_t ws_bytes;
+  // Byte ranges [off, off + bytes) that must be zero before a call (the library leaves
+  // them zeroed after every call that completes without a device error).
+  size_t zero_off[2], zero_bytes[2];
 };
 
 int make_plan(const tfa_fwd_params* p, int device, FullPlan* fp) {
@@ -186,13 +212,24 @@ int make_plan(const tfa_fwd_params* p, int device, FullPlan* fp) {
   fp->mixed = (fp->pre.kernel == 1 && p->batch >= kMixedMinBatch && G <= 16) ? 1 : 0;
   fp->dec_off = 0;
   fp->ws_bytes = fp->pre.ws_bytes;
+  fp->zero_off[0] = 0;
+  fp->zero_bytes[0] = fp->pre.zero_bytes;
+  fp->zero_off[1] = fp->zero_bytes[1] = 0;
   if (fp->mixed) {
     tfa_fwd_params d = *p;
     d.max_seqlen_q = 16 / G;  // the decode kernel's sequences are at most this long
     if ((rc = make_plan_one(&d, device, &fp->dec)) != TFA_OK) return rc;
     fp->dec.item_list = 0;  // the decode part of a mixed call keeps slot order
+    if (fp->dec.ws_bytes > fp->dec.list_off && fp->dec.list_off) fp->dec.ws_bytes = fp->dec.list_off;
+    // the decode part counts its groups in the call's own counter region, so the call
+    // reserves it whenever the decode part has splits
+    if (fp->dec.combine == 2 && fp->pre.ws_bytes < kCounterRegionEnd) {
+      fp->pre.ws_bytes = kCounterRegionEnd;
+      fp->pre.zero_bytes = kCounterRegionEnd;
+    }
     fp->dec_off = align_up(fp->pre.ws_bytes, 256);
     fp->ws_bytes = fp->dec_off + fp->dec.ws_bytes;
+    fp->zero_bytes[0] = fp->pre.zero_bytes;
   }
   return TFA_OK;
 }
@@ -241,10 +278,10 @@ void fill_params(const tfa_fwd_params* a, const Plan& pl, void* ws, FwdParams* p
     p->item_count = reinterpret_cast<const int*>(w) + 6;  // control word 6, written by the list kernel
   }
   if (pl.max_splits > 1) {
-    const size_t rows = (size_t)pl.max_splits * a->total_q * a->num_q_heads;
-    p->split_lse = reinterpret_cast<float*>(w + kCtrlBytes);
-    p->split_o = reinterpret_cast<float*>(w + kCtrlBytes + align_up(rows * sizeof(float), 256));
+    p->split_lse = reinterpret_cast<float*>(w + pl.lse_off);
+    p->split_o = reinterpret_cast<float*>(w + pl.o_off);
   }
+  if (pl.combine == 2) p->group_cnt = reinterpret_cast<int*>(w + pl.cnt_off);
 }
 
 int encode_maps(const tfa_fwd_params* a, int box_rows, KvMaps* m) {
@@ -315,6 +352,7 @@ int tfa_plan(const tfa_fwd_params* p, int device, tfa_plan_info* info) {
   info->grid = pl.grid;
   info->combine = pl.combine;
   info->workspace_bytes = fp.ws_bytes;
+  info->item_list = pl.item_list;
   return TFA_OK;
 }
 
@@ -328,6 +366,18 @@ size_t tfa_workspace_size(const tfa_fwd_params* p, int device) {
 }  // extern "C"
 
 namespace tfa {
+int workspace_zero_ranges(const tfa_fwd_params* p, int device, size_t off[2], size_t bytes[2]) {
+  int rc = validate(p);
+  if (rc != TFA_OK) return rc;
+  FullPlan fp;
+  if ((rc = make_plan(p, device, &fp)) != TFA_OK) return rc;
+  for (int i = 0; i < 2; ++i) {
+    off[i] = fp.zero_off[i];
+    bytes[i] = fp.zero_bytes[i];
+  }
+  return TFA_OK;
+}
+
 // Shared by every forward entry point: checks, plan, descriptors, launches.
 int fwd_impl(const tfa_fwd_params* a, void* workspace, size_t workspace_bytes, void* stream, void* ev_begin,
              void* ev_end) {
@@ -354,6 +404,8 @@ int fwd_impl(const tfa_fwd_params* a, void* workspace, size_t workspace_bytes, v
     // kernel's scheduler counters are its words 4-5, the error word is shared.
     pd.sched = p.sched + 4;
     pd.err = p.err;
+    // the call's counter region (the prefill part merges with the combine kernel)
+    if (pd.group_cnt) pd.group_cnt = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(workspace) + kCtrlBytes);
     pd.debug_stall = p.debug_stall;
     p.seq_filter = 2;
     pd.seq_filter = 1;
@@ -390,12 +442,12 @@ int fwd_impl(const tfa_fwd_params* a, void* workspace, size_t workspace_bytes, v
   if (e != cudaSuccess) return fail(e);
   if (ev_end && cudaEventRecord(reinterpret_cast<cudaEvent_t>(ev_end), s) != cudaSuccess) return TFA_ERR_CUDA;
   const int64_t G = a->num_q_heads / a->num_kv_heads;
-  if (fp.mixed && fp.dec.combine) {
+  if (fp.mixed && fp.dec.combine == 1) {
     const int64_t rows = std::min<int64_t>(fp.dec.rows, (16 / G) * G);
     e = a->head_dim == 64 ? launch_combine<64>(pd, (int)rows, s) : launch_combine<128>(pd, (int)rows, s);
     if (e != cudaSuccess) return fail(e);
   }
-  if (pl.combine) {
+  if (pl.combine == 1) {
     // packed rows per group: at most one q tile, at most the longest query times the group
     const int64_t rows = std::min<int64_t>(pl.rows, a->max_seqlen_q * G);
     e = a->head_dim == 64 ? launch_combine<64>(p, (int)rows, s) : launch_combine<128>(p, (int)rows, s);

@@ -35,12 +35,17 @@ constexpr int kNP = 16;  // packed q rows (MMA N)
 
 #ifdef TFA_PROFILE
 __device__ unsigned long long g_decode_stamp[32];
+__device__ unsigned long long g_decode_tile[16][12];
+__device__ unsigned long long g_decode_end[512];
 #define STAMP(i) do { if (blockIdx.x == 0) g_decode_stamp[i] = global_timer_ns(); } while (0)
+#define PH(cj, i) do { if (blockIdx.x == 0 && (cj) < 16) g_decode_tile[cj][i] = global_timer_ns(); } while (0)
 }  // namespace
 __device__ void decode_stamp_hook(int i) { g_decode_stamp[i] = global_timer_ns(); }
+__device__ void decode_tile_hook(int c, int i) { if (blockIdx.x == 0 && c < 16) g_decode_tile[c][i] = global_timer_ns(); }
 namespace {
 #else
 #define STAMP(i) do {} while (0)
+#define PH(cj, i) do {} while (0)
 #endif
 
 template <int D>
@@ -64,6 +69,74 @@ struct DecodeCfg {
   static constexpr uint32_t kTmemCols = 64;              // S^T x2 (16 cols), O^T x2 (16 cols)
 };
 
+// Merges the split partials of work group w (all of its splits have finished and
+// published their rows) into `out` and the LSE: out = sum_s 2^(lse_s - M) o_s / sum_s
+// 2^(lse_s - M), M = max_s lse_s (the LSE merge of v8/flash_attn_func.cu:701-777, in an
+// online form over chunks of eight splits). Run by the 128 softmax threads of the CTA
+// whose split finished last: D / 4 threads per row, four columns each, so a pass covers
+// 512 / D rows; every load of a chunk is issued before any is used (one L2 round trip
+// per chunk). Partials are read with L1-bypassing loads (other CTAs wrote them).
+template <int D>
+__device__ __forceinline__ void merge_splits(const FwdParams& p, const Work& w, int tq) {
+  constexpr int kTpr = D / 4;        // threads per row
+  constexpr int kRpp = 128 / kTpr;   // rows per pass
+  constexpr int kChunk = 8;
+  const int64_t stride = (int64_t)p.total_q * p.hq;
+  const int c4 = (tq % kTpr) * 4;
+  const int ns = w.nsplits;
+  for (int r = tq / kTpr; r < w.nrows; r += kRpp) {
+    const int R = w.row0 + r;
+    const int tok = w.q0 + R / p.group;
+    const int qh = w.h * p.group + R % p.group;
+    const int64_t pair = (int64_t)tok * p.hq + qh;
+    float mx = -INFINITY, wsum = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s0 = 0; s0 < ns; s0 += kChunk) {
+      float ls[kChunk];
+      float4 ov[kChunk];
+#pragma unroll
+      for (int i = 0; i < kChunk; ++i) {
+        const int s = s0 + i;
+        if (s < ns) {
+          ls[i] = __ldcg(p.split_lse + s * stride + pair);
+          ov[i] = __ldcg(reinterpret_cast<const float4*>(p.split_o + (s * stride + pair) * D + c4));
+        } else {
+          ls[i] = -INFINITY;
+          ov[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+      float cm = mx;
+#pragma unroll
+      for (int i = 0; i < kChunk; ++i) cm = fmaxf(cm, ls[i]);
+      if (cm == -INFINITY) continue;
+      const float sc = (mx == -INFINITY) ? 0.f : ex2_approx(mx - cm);
+      wsum *= sc;
+      acc.x *= sc;
+      acc.y *= sc;
+      acc.z *= sc;
+      acc.w *= sc;
+#pragma unroll
+      for (int i = 0; i < kChunk; ++i) {
+        const float wl = (ls[i] == -INFINITY) ? 0.f : ex2_approx(ls[i] - cm);
+        wsum += wl;
+        acc.x += wl * ov[i].x;
+        acc.y += wl * ov[i].y;
+        acc.z += wl * ov[i].z;
+        acc.w += wl * ov[i].w;
+      }
+      mx = cm;
+    }
+    const float inv = (mx == -INFINITY) ? 0.f : 1.f / wsum;
+    __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
+    __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
+    uint2 packed;
+    packed.x = *reinterpret_cast<uint32_t*>(&lo);
+    packed.y = *reinterpret_cast<uint32_t*>(&hi);
+    *reinterpret_cast<uint2*>(p.out + (int64_t)tok * p.o_s0 + (int64_t)qh * p.o_s1 + c4) = packed;
+    if (c4 == 0 && p.lse) p.lse[pair] = (mx == -INFINITY) ? -INFINITY : (mx + lg2_approx(wsum)) * kLn2;
+  }
+}
+
 template <int D, bool kList>
 __global__ void __launch_bounds__(224, 1)
     decode_kernel(const __grid_constant__ FwdParams p, const __grid_constant__ KvMaps maps,
@@ -86,11 +159,23 @@ __global__ void __launch_bounds__(224, 1)
   __shared__ uint64_t stall_bar;  // never arrived on: the time-limit test hook waits here
   __shared__ __align__(16) float red_max[2][4][kNP];
   __shared__ __align__(16) float red_sum[2][4][kNP];
+  __shared__ int merge_flag[2];
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
   if (tid == 0) STAMP(0);
+  if constexpr (!kList) {
+    // The first item of this CTA is item blockIdx.x: bring its sequence's lengths and the
+    // start of its block-table row into L2 while the CTA sets up (the producer's first
+    // loads then hit L2 instead of waiting a DRAM round trip after the prologue).
+    if (warp == 0 && lane < 3) {
+      const int b = (int)((blockIdx.x / (unsigned)p.hkv) % (unsigned)p.batch);
+      const void* a = lane == 0 ? (const void*)(p.cu_seqlens_q + b)
+                    : lane == 1 ? (const void*)(p.seqused_k + b) : (const void*)(p.block_table + (int64_t)b * p.bt_s0);
+      prefetch_l2(a);
+    }
+  }
 
   if (tid == 0) {
     for (int i = 0; i < Cfg::kKSlots; ++i) {
@@ -170,6 +255,7 @@ __global__ void __launch_bounds__(224, 1)
           }
           umma_commit(&empty_k[st]);  // frees the K slot once QK has read it
           umma_commit(&s_full[cc & 1]);
+          PH(cc, 2);
         };
         auto issue_pv = [&](int cj) {
           tc_fence_after();
@@ -186,6 +272,7 @@ __global__ void __launch_bounds__(224, 1)
           }
           umma_commit(&empty_v[st]);  // frees the V slot once this P.V has read it
           umma_commit(&o_full[cj & 1]);
+          PH(cj, 3);
         };
         // QK of tile jq and P.V of tile jp are issued as soon as each one's inputs are
         // ready, in whichever order that happens: a P.V (which frees its stage) never
@@ -298,12 +385,14 @@ __global__ void __launch_bounds__(224, 1)
         }
         tc_fence_after();
         if (warp == 2 && lane == 0 && cj == 0) STAMP(8);
+        if (warp == 2 && lane == 0) PH(cj, 4);
         float s[kNP];
         tmem_ld16(lane_base + (cj & 1) * kNP, s);
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&s_free[cj & 1]);
+        if (warp == 2 && lane == 0) PH(cj, 5);
 
         const int pos = (w.tile_begin + j) * kBN + tl;
         float a[kNP];
@@ -316,10 +405,12 @@ __global__ void __launch_bounds__(224, 1)
           const float wm = col16_reduce<true>(t, lane);
           if ((lane & 1) == 0) red_max[cj & 1][sw][col16_of_lane(lane)] = wm;
         }
+        if (warp == 2 && lane == 0) PH(cj, 6);
         if (!sm_sync()) {
           ok = false;
           break;
         }
+        if (warp == 2 && lane == 0) PH(cj, 7);
         float cmax[kNP];
 #pragma unroll
         for (int q4 = 0; q4 < kNP / 4; ++q4) {
@@ -342,6 +433,7 @@ __global__ void __launch_bounds__(224, 1)
           l[r] = l[r] * a[r] + s[r];
           m[r] = mn;
         }
+        if (warp == 2 && lane == 0) PH(cj, 8);
         // fold the previous tile's P.V into the register accumulator
         if (j > 0) {
           const int cp = cj - 1;
@@ -349,6 +441,7 @@ __global__ void __launch_bounds__(224, 1)
             ok = false;
             break;
           }
+          if (warp == 2 && lane == 0) PH(cj, 9);
           tc_fence_after();
           float ot[kNP];
           tmem_ld16(lane_base + 32 + (cp & 1) * kNP, ot);
@@ -359,6 +452,7 @@ __global__ void __launch_bounds__(224, 1)
 #pragma unroll
           for (int r = 0; r < kNP; ++r) o[r] = o[r] * a_prev[r] + ot[r];
         }
+        if (warp == 2 && lane == 0) PH(cj, 10);
 #pragma unroll
         for (int r = 0; r < kNP; ++r) a_prev[r] = a[r];
         // P^T -> shared memory: row r (q row), column tl (kv token), K-major SW128.
@@ -371,6 +465,7 @@ __global__ void __launch_bounds__(224, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[cj & 1]);
         if (warp == 2 && lane == 0 && cj == 0) STAMP(9);
+        if (warp == 2 && lane == 0) PH(cj, 11);
       }
       if (ok && n > 0) {
         const int cl = c + n - 1;
@@ -437,6 +532,24 @@ __global__ void __launch_bounds__(224, 1)
         }
         if (warp == 2 && lane == 0 && k == 0 && r == 0) STAMP(17);
       }
+      if (!direct) {
+        // Split combine inside the kernel: every split publishes its rows, then counts
+        // itself done for the group; the split that completes the count merges them all
+        // (and resets the count for the next launch).
+        __threadfence();
+        if (!sm_sync()) break;
+        if (sw == 0 && lane == 0) {
+          const int done = atomicAdd(&p.group_cnt[w.g], 1);
+          const int last = done == w.nsplits - 1 ? 1 : 0;
+          if (last) {
+            atomicExch(&p.group_cnt[w.g], 0);
+            __threadfence();
+          }
+          merge_flag[k & 1] = last;
+        }
+        if (!sm_sync()) break;
+        if (merge_flag[k & 1]) merge_splits<D>(p, w, tq);
+      }
       __syncwarp();
       if (warp == 2 && lane == 0 && k == 0) STAMP(11);
       if (lane == 0) mbar_arrive(&item_empty[slot]);
@@ -458,6 +571,9 @@ __global__ void __launch_bounds__(224, 1)
     tmem_dealloc(tmem, Cfg::kTmemCols);
   }
   if (tid == 0) STAMP(14);
+#ifdef TFA_PROFILE
+  if (tid == 0 && blockIdx.x < 512) g_decode_end[blockIdx.x] = global_timer_ns();
+#endif
 }
 
 }  // namespace
@@ -490,6 +606,13 @@ cudaError_t launch_decode(const FwdParams& p, const KvMaps& maps, const CUtensor
 #ifdef TFA_PROFILE
 extern "C" __attribute__((visibility("default"))) int tfa_decode_stamps_read(unsigned long long* host) {
   return (int)cudaMemcpyFromSymbol(host, g_decode_stamp, sizeof(g_decode_stamp));
+}
+extern "C" __attribute__((visibility("default"))) int tfa_decode_tiles_read(unsigned long long* host) {
+  return (int)cudaMemcpyFromSymbol(host, g_decode_tile, sizeof(g_decode_tile));
+}
+extern "C" __attribute__((visibility("default"))) int tfa_decode_ends_read(unsigned long long* host) {
+  cudaError_t e = cudaMemcpyFromSymbol(host, g_decode_end, sizeof(g_decode_end));
+  return (int)e;
 }
 #endif
 

@@ -13,4 +13,8 @@ namespace tfa {
 int fwd_impl(const tfa_fwd_params* a, void* workspace, size_t workspace_bytes, void* stream, void* ev_begin,
              void* ev_end);
 
+// Byte ranges [off[i], off[i] + bytes[i]) of this call's workspace that must be zero
+// when it starts (the control block and the decode kernel's split counters).
+int workspace_zero_ranges(const tfa_fwd_params* p, int device, size_t off[2], size_t bytes[2]);
+
 }  // namespace tfa

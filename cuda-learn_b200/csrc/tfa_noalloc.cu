@@ -70,8 +70,29 @@ extern "C" int tfa_fwd_static_workspace(const tfa_fwd_params* p, void* stream) {
   void* ws = nullptr;
   int rc = static_workspace_for_current_device(&ws);
   if (rc != TFA_OK) return rc;
-  // The scheduler counters and the error word must start at zero; the split partials
-  // are fully written before they are read, so only the 256-byte control block is cleared.
-  if (cudaMemsetAsync(ws, 0, 256, reinterpret_cast<cudaStream_t>(stream)) != cudaSuccess) return TFA_ERR_CUDA;
+  // The scheduler counters, the error word and the decode kernel's per-group split
+  // counters must start at zero; the split partials are fully written before they are
+  // read, so only those leading ranges are cleared.
+  size_t off[2], bytes[2];
+  if ((rc = workspace_zero_ranges(p, dev, off, bytes)) != TFA_OK) return rc;
+  for (int i = 0; i < 2; ++i)
+    if (bytes[i] && cudaMemsetAsync(static_cast<unsigned char*>(ws) + off[i], 0, bytes[i],
+                                    reinterpret_cast<cudaStream_t>(stream)) != cudaSuccess)
+      return TFA_ERR_CUDA;
   return fwd_impl(p, ws, TFA_STATIC_WORKSPACE_BYTES, stream, nullptr, nullptr);
+}
+
+extern "C" int tfa_read_static_workspace_error(void* stream, int* err) {
+  using namespace tfa;
+  if (!err) return TFA_ERR_NULL_POINTER;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return TFA_ERR_CUDA;
+  if (dev < 0 || dev >= kMaxDevices) return TFA_ERR_DEVICE;
+  void* ws = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_workspace_mutex);
+    ws = g_workspace_addr[dev];
+  }
+  if (!ws) return TFA_ERR_CUDA;
+  return tfa_read_device_error(ws, stream, err);
 }

@@ -36,6 +36,7 @@ EXPORTED_SYMBOLS = (
     "tfa_fwd",
     "tfa_fwd_timed",
     "tfa_fwd_static_workspace",
+    "tfa_read_static_workspace_error",
     "tfa_read_device_error",
     "tfa_device_sm_count",
     "tfa_status_string",
@@ -95,6 +96,7 @@ class TfaPlanInfo(ctypes.Structure):
         ("grid", _i32),
         ("combine", _i32),
         ("workspace_bytes", ctypes.c_uint64),
+        ("item_list", _i32),
     ]
 
 
@@ -131,6 +133,8 @@ def load() -> ctypes.CDLL:
         lib.tfa_fwd_timed.restype = ctypes.c_int
         lib.tfa_fwd_static_workspace.argtypes = [P(TfaFwdParams), _vp]
         lib.tfa_fwd_static_workspace.restype = ctypes.c_int
+        lib.tfa_read_static_workspace_error.argtypes = [_vp, P(ctypes.c_int)]
+        lib.tfa_read_static_workspace_error.restype = ctypes.c_int
         lib.tfa_read_device_error.argtypes = [_vp, _vp, P(ctypes.c_int)]
         lib.tfa_read_device_error.restype = ctypes.c_int
         lib.tfa_device_sm_count.argtypes = [ctypes.c_int]

@@ -23,7 +23,7 @@ from dataclasses import dataclass, replace
 import torch
 
 __all__ = ["PagedCase", "reference_case", "baseline_config", "c5_kv_lengths", "BASELINE_CONFIGS", "kv_bytes",
-           "prefill_flops"]
+           "prefill_flops", "compact_sample", "verify_sequences"]
 
 
 @dataclass
@@ -165,12 +165,15 @@ def baseline_config(
     kv_range: tuple[int, int] | None = None,
     kv_heads: int | None = None,
     q_heads: int | None = None,
+    value_seed: int | None = None,
 ) -> PagedCase:
     """Builds configuration C1..C5. Overrides shrink a configuration for tests
     (``batch``, pool ``num_blocks``, ``kv_range``) or shard it (``kv_heads``/``q_heads``).
 
-    Lengths and block tables are drawn from a CPU generator (the same on every device);
-    q/K/V values from a generator on ``device``."""
+    Lengths and block tables are drawn from a CPU generator seeded with ``seed`` (the
+    same on every device); q/K/V values from a generator on ``device`` seeded with
+    ``value_seed`` (default ``seed``), so the shards of one configuration can share
+    lengths and tables but hold different values."""
     name = name.upper()
     seed = {"C1": 1, "C2": 2, "C3": 3, "C4": 4, "C5": 5, "P1": 11, "P2": 12}[name] if seed is None else seed
     dev = torch.device(device)
@@ -229,7 +232,7 @@ def baseline_config(
         o += n
     if kv_heads is not None:
         hq, hkv = (q_heads if q_heads is not None else hq * kv_heads // hkv), kv_heads
-    g = torch.Generator(device=dev).manual_seed(seed + 1000)
+    g = torch.Generator(device=dev).manual_seed((seed if value_seed is None else value_seed) + 1000)
     total_q = sum(q_lens)
     q = _fill_randn_(torch.empty(total_q, hq, d, dtype=torch.bfloat16, device=dev), g)
     k_cache = _fill_randn_(torch.empty(nb, bs, hkv, d, dtype=torch.bfloat16, device=dev), g)
@@ -283,3 +286,46 @@ def prefill_flops(case: PagedCase) -> int:
     """4 * d * Hq * (number of unmasked (query, key) pairs)."""
     hq, d = case.q.shape[1], case.q.shape[2]
     return 4 * d * hq * sum(sum(rows) for rows in attended(case))
+
+
+def compact_sample(case: PagedCase, seqs: list[int], device=None) -> PagedCase:
+    """The sequences ``seqs`` of ``case`` as a case of their own: q rows, lengths and only
+    their live cache blocks, renumbered densely (block i of the sample is the i-th live
+    block of the listed sequences, in order). The gather runs where ``case`` lives; the
+    result is moved to ``device`` (default: stays there). Used to check a sample of a
+    large call against a CPU reference without copying its whole pool."""
+    dev = case.q.device
+    cu = case.cu_seqlens_q.tolist()
+    used = case.seqused_k.tolist()
+    bs = case.k_cache.shape[1]
+    need = [(used[b] + bs - 1) // bs for b in seqs]
+    rows = [case.block_table[b, :n].long() for b, n in zip(seqs, need)]
+    ids = torch.cat(rows) if rows else torch.empty(0, dtype=torch.long, device=dev)
+    k = case.k_cache[ids]
+    v = case.v_cache[ids]
+    if k.shape[0] == 0:
+        k = torch.zeros((1,) + tuple(case.k_cache.shape[1:]), dtype=case.k_cache.dtype, device=dev)
+        v = torch.zeros_like(k)
+    table = torch.full((len(seqs), max(max(need, default=1), 1)), -1, dtype=torch.int32)
+    o = 0
+    for i, n in enumerate(need):
+        table[i, :n] = torch.arange(o, o + n, dtype=torch.int32)
+        o += n
+    q = torch.cat([case.q[cu[b]:cu[b + 1]] for b in seqs]) if seqs else case.q[:0]
+    q_lens = [cu[b + 1] - cu[b] for b in seqs]
+    out = PagedCase(f"{case.name}[{len(seqs)} seqs]", q, k, v, _cu(q_lens), torch.tensor([used[b] for b in seqs],
+                    dtype=torch.int32), table, max(q_lens, default=0), max((used[b] for b in seqs), default=0),
+                    case.causal, case.window_size)
+    return out.to(device if device is not None else dev)
+
+
+def verify_sequences(kv_lens: list[int], n_longest: int = 16, n_random: int = 16, seed: int = 77) -> list[int]:
+    """Sequence indices of the verification sample of a large decode call: the
+    ``n_longest`` longest sequences plus ``n_random`` others drawn with a fixed seed,
+    sorted."""
+    order = sorted(range(len(kv_lens)), key=lambda b: (-kv_lens[b], b))
+    longest = order[:n_longest]
+    rest = order[n_longest:]
+    g = torch.Generator().manual_seed(seed)
+    pick = torch.randperm(len(rest), generator=g)[:n_random].tolist()
+    return sorted(longest + [rest[i] for i in pick])

@@ -99,8 +99,12 @@ typedef struct tfa_plan_info {
   int32_t split_cap;      /* kv tiles (128 tokens) per split, at most */
   int32_t num_items;      /* work-item slots (unused split slots are skipped on device) */
   int32_t grid;           /* persistent CTAs launched */
-  int32_t combine;        /* 1 if the LSE combine kernel runs after the main kernel */
+  int32_t combine;        /* how split partials are merged: 0 = no splits, 1 = by the LSE combine
+                             kernel launched after the prefill kernel, 2 = inside the decode kernel
+                             (the last split of each group to finish merges the group) */
   uint64_t workspace_bytes;
+  int32_t item_list;      /* 1 if the decode kernel takes its items from a list built on the
+                             device for the call (longest first; one extra small kernel) */
 } tfa_plan_info;
 
 /* Fills *info for the call described by p on CUDA device `device` (device < 0: plan for
@@ -136,11 +140,18 @@ TFA_API int tfa_fwd_timed(const tfa_fwd_params* p, void* workspace, size_t works
  * (tfa_workspace_size) return TFA_ERR_STATIC_WORKSPACE_LIMIT. All calls on a device share
  * the array, so calls that can overlap on the GPU race and must not be issued. The first
  * call on a device looks up the array's address with that device current and should come
- * before any stream capture. Error words are read with tfa_read_device_error only for
- * caller-owned workspaces, so this entry's kernel errors are not reported.
+ * before any stream capture. Kernel errors of these calls land in the array's error word,
+ * which tfa_read_static_workspace_error reads.
  * No counterpart in the reference (its op allocates its split buffers on every call,
  * v8/flash_attn_func.cu:850-862). */
 TFA_API int tfa_fwd_static_workspace(const tfa_fwd_params* p, void* stream);
+
+/* tfa_read_device_error for the library-owned workspace of tfa_fwd_static_workspace on the
+ * current device: synchronises `stream`, copies the error word into *err (0 = none) and
+ * clears it (the next tfa_fwd_static_workspace call also starts from a cleared control
+ * block). Returns TFA_ERR_CUDA if no tfa_fwd_static_workspace call has run on this device.
+ * No counterpart in the reference. */
+TFA_API int tfa_read_static_workspace_error(void* stream, int* err);
 
 /* Synchronises `stream`, copies the device error word of `workspace` into *err (0 = none)
  * and clears it. A non-zero word means a kernel hit an internal time limit (codes

@@ -110,7 +110,7 @@ def test_plan_without_gpu_uses_b200_sm_count():
     info = _lib.TfaPlanInfo()
     assert _lib.load().tfa_plan(ctypes.byref(p), -1, ctypes.byref(info)) == 0
     assert info.kernel == 0 and info.rows_per_tile == 16
-    assert info.max_splits == 16 and info.split_cap == 1 and info.combine == 1
+    assert info.max_splits == 16 and info.split_cap == 1 and info.combine == 2  # merged in the decode kernel
     assert info.grid == min(info.num_items, 148)
     p.max_seqlen_q = 128
     assert _lib.load().tfa_plan(ctypes.byref(p), -1, ctypes.byref(info)) == 0
@@ -128,7 +128,9 @@ def test_workspace_size_grows_with_splits():
     p.num_splits = 8
     eight = lib.tfa_workspace_size(ctypes.byref(p), -1)
     assert one == 256 and eight > one
-    assert eight == 256 + ((8 * 4 * 4 * 4 + 255) // 256) * 256 + 8 * 4 * 4 * 64 * 4
+    # control block and the fixed 64 KB region of the decode kernel's split counters, then
+    # split LSEs and split outputs
+    assert eight == 65536 + ((8 * 4 * 4 * 4 + 255) // 256) * 256 + 8 * 4 * 4 * 64 * 4
 
 
 def test_python_wrapper_rejects_cpu_tensors():

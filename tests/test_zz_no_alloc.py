@@ -7,7 +7,9 @@ workspace. This file runs last so a failure here never hides the other tests; it
 passes when run alone in a fresh process.
 
 Check: two calls in a row through the C ABI must agree with the caller-workspace entry
-point ``tfa_fwd`` within the parity tolerance (2e-2 on the output, 1e-3 on the LSE).
+point ``tfa_fwd`` and with the CPU oracle within the parity tolerance (2e-2 on the output,
+1e-3 on the LSE); kernel errors of these calls are read back with
+``tfa_read_static_workspace_error``.
 """
 
 from __future__ import annotations
@@ -17,6 +19,7 @@ import ctypes
 import pytest
 import torch
 
+from oracle.paged_attention import paged_attention_oracle
 from toy_flash_attn import _lib
 from toy_flash_attn import flash_attention_func as faf
 from toy_flash_attn.workloads import baseline_config, reference_case
@@ -31,6 +34,21 @@ STATIC_WS_BYTES = 32 * 1024 * 1024
 def _params(c, out, lse, num_splits=0):
     return faf._fill_params(c.q, c.k_cache, c.v_cache, out, c.cu_seqlens_q, c.seqused_k, c.block_table,
                             c.max_seqlen_q, c.max_seqlen_k, c.causal, c.window_size, lse, None, num_splits)
+
+
+def _static_error() -> int:
+    err = ctypes.c_int(-1)
+    _lib.check(_lib.load().tfa_read_static_workspace_error(torch.cuda.current_stream().cuda_stream,
+                                                           ctypes.byref(err)), "tfa_read_static_workspace_error")
+    return err.value
+
+
+def _item_list_case():
+    g = torch.Generator().manual_seed(31)
+    k_lens = [int(x) for x in torch.exp(torch.empty(48).uniform_(0, 8.3, generator=g)).round().clamp(1, 4096)]
+    k_lens[0] = 4096
+    return reference_case([1] * 48, k_lens, num_heads=16, num_kv_heads=4, head_dim=128, causal=True, block_size=16,
+                          seed=31)
 
 
 def _static_call(c, num_splits=0):
@@ -52,26 +70,42 @@ def _static_call(c, num_splits=0):
         (lambda: baseline_config("C4", batch=8), 0),        # sliding window, NaN cache slots
         (lambda: reference_case([1, 9], [700, 90], num_heads=8, num_kv_heads=2, head_dim=128, causal=True,
                                 block_size=16, seed=3), 0),
+        (_item_list_case, 0),                                # decode kernel with the device-built item list
     ],
-    ids=["C2", "C3_split3", "C4_b8", "hd128_mixed"],
+    ids=["C2", "C3_split3", "C4_b8", "hd128_mixed", "item_list"],
 )
 def test_static_workspace_matches_tfa_fwd_twice(make, splits):
-    c = make().to("cuda")
+    case = make()
+    c = case.to("cuda")
     ref_out = torch.empty_like(c.q)
     ref_lse = torch.empty(c.q.shape[0], c.q.shape[1], dtype=torch.float32, device="cuda")
     faf.flash_attn_varlen_func(**c.kwargs(), out=ref_out, softmax_lse=ref_lse, num_splits=splits)
     torch.cuda.synchronize()
+    cpu_out, cpu_lse = paged_attention_oracle(case.q, case.k_cache, case.v_cache, case.cu_seqlens_q,
+                                              case.seqused_k, case.block_table, case.causal, case.window_size)
     for _ in range(2):  # the array keeps the previous call's contents; results must not depend on it
         out, lse = _static_call(c, splits)
+        assert _static_error() == 0
         assert torch.isfinite(out.float()).all()
-        assert (out.float() - ref_out.float()).abs().max().item() <= OUT_TOL
-        fin = torch.isfinite(ref_lse)
-        assert torch.equal(fin, torch.isfinite(lse))
-        assert (lse[fin] - ref_lse[fin]).abs().max().item() <= LSE_TOL
+        for want_out, want_lse in ((ref_out.float(), ref_lse), (cpu_out.to("cuda"), cpu_lse.to("cuda"))):
+            assert (out.float() - want_out).abs().max().item() <= OUT_TOL
+            fin = torch.isfinite(want_lse)
+            assert torch.equal(fin, torch.isfinite(lse))
+            assert (lse[fin] - want_lse[fin]).abs().max().item() <= LSE_TOL
+
+
+def test_static_workspace_reports_bad_block_id():
+    case = reference_case([1], [40], num_heads=2, num_kv_heads=1, block_size=16)
+    case.block_table[0, 1] = 10_000  # outside the pool: read as zeros and reported as error 110
+    c = case.to("cuda")
+    _static_call(c)
+    assert _static_error() == 110
+    assert _static_error() == 0  # cleared
 
 
 def test_static_workspace_rejects_oversized_call():
-    # 2048 sequences x 32 q heads x 16 splits x 128 dims of fp32 partials >> 32 MiB
+    # 64 sequences x 32 q heads x 32 splits x 128 dims of fp32 partials = 32 MiB, plus the LSEs and
+    # the control block: more than the static array holds
     c = reference_case([1] * 64, [4096] * 64, num_heads=32, num_kv_heads=8, head_dim=128, causal=True,
                        block_size=16).to("cuda")
     out = torch.empty_like(c.q)
