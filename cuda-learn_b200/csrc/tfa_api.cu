@@ -150,12 +150,15 @@ int make_plan_one(const tfa_fwd_params* p, int device, Plan* pl) {
   pl->num_items = (int)items;
   pl->grid = (int)(items < sms ? items : sms);
   if (pl->grid < 1) pl->grid = 1;
-  // Split partials are merged by the decode kernel itself (the last split of a group to
-  // finish, counted per group in the reserved counter region) or, after the prefill
-  // kernel and for decode calls with more groups than the region counts, by the combine
-  // kernel.
+  // Split partials of small (latency-bound) decode calls are merged inside the decode
+  // kernel by the last split of each group to finish, counted per group in the reserved
+  // counter region: that saves the combine kernel's launch and its wait for the whole
+  // grid. Large decode calls and prefill calls merge with the combine kernel, which then
+  // overlaps the attention kernel's tail; on a bandwidth-bound call the per-split fence,
+  // count and merge inside the kernel cost more (C5 on one B200: +3.7 % per call).
   const int64_t groups = (int64_t)p->batch * p->num_kv_heads * pl->q_tiles;
-  pl->combine = S > 1 ? ((decode && groups <= kMaxCountedGroups) ? 2 : 1) : 0;
+  const bool latency_bound = est_all < 32 * (int64_t)sms;
+  pl->combine = S > 1 ? ((decode && latency_bound && groups <= kMaxCountedGroups) ? 2 : 1) : 0;
   size_t ws = kCtrlBytes;
   pl->cnt_off = pl->lse_off = pl->o_off = 0;
   if (S > 1) {
@@ -176,7 +179,8 @@ int make_plan_one(const tfa_fwd_params* p, int device, Plan* pl) {
   // Used where the grid's tail weighs: under ~1024 tiles per SM of the max-length bound
   // (a C5 shard at 4 or 8 GPUs: -4.6 % per call); on larger calls the extra launch costs
   // more than the tail it saves.
-  pl->item_list = (decode && S > 1 && items > 2 * (int64_t)sms && est_all < 1024 * (int64_t)sms) ? 1 : 0;
+  pl->item_list =
+      (decode && pl->combine == 1 && items > 2 * (int64_t)sms && est_all < 1024 * (int64_t)sms) ? 1 : 0;
   pl->list_off = 0;
   if (pl->item_list) {
     pl->list_off = align_up(ws, 256);
@@ -405,7 +409,7 @@ int fwd_impl(const tfa_fwd_params* a, void* workspace, size_t workspace_bytes, v
     pd.sched = p.sched + 4;
     pd.err = p.err;
     // the call's counter region (the prefill part merges with the combine kernel)
-    if (pd.group_cnt) pd.group_cnt = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(workspace) + kCtrlBytes);
+    if (fp.dec.combine == 2) pd.group_cnt = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(workspace) + kCtrlBytes);
     pd.debug_stall = p.debug_stall;
     p.seq_filter = 2;
     pd.seq_filter = 1;
@@ -427,18 +431,20 @@ int fwd_impl(const tfa_fwd_params* a, void* workspace, size_t workspace_bytes, v
   };
   if (ev_begin && cudaEventRecord(reinterpret_cast<cudaEvent_t>(ev_begin), s) != cudaSuccess) return TFA_ERR_CUDA;
   if (fp.mixed) {
-    e = a->head_dim == 64 ? launch_decode<64>(pd, maps, q_map, fp.dec.grid, s)
-                          : launch_decode<128>(pd, maps, q_map, fp.dec.grid, s);
+    const int mode = fp.dec.combine == 2 ? 2 : 0;
+    e = a->head_dim == 64 ? launch_decode<64>(pd, maps, q_map, fp.dec.grid, s, mode)
+                          : launch_decode<128>(pd, maps, q_map, fp.dec.grid, s, mode);
     if (e != cudaSuccess) return fail(e);
   }
   if (pl.kernel == 0 && pl.item_list) {
     e = launch_item_list(p, const_cast<int*>(p.item_list), const_cast<int*>(p.item_count), s);
     if (e != cudaSuccess) return fail(e);
   }
+  const int mode = pl.item_list ? 1 : (pl.combine == 2 ? 2 : 0);  // decode kernel instance
   if (a->head_dim == 64)
-    e = pl.kernel == 0 ? launch_decode<64>(p, maps, q_map, pl.grid, s) : launch_prefill<64>(p, maps, pl.grid, s);
+    e = pl.kernel == 0 ? launch_decode<64>(p, maps, q_map, pl.grid, s, mode) : launch_prefill<64>(p, maps, pl.grid, s);
   else
-    e = pl.kernel == 0 ? launch_decode<128>(p, maps, q_map, pl.grid, s) : launch_prefill<128>(p, maps, pl.grid, s);
+    e = pl.kernel == 0 ? launch_decode<128>(p, maps, q_map, pl.grid, s, mode) : launch_prefill<128>(p, maps, pl.grid, s);
   if (e != cudaSuccess) return fail(e);
   if (ev_end && cudaEventRecord(reinterpret_cast<cudaEvent_t>(ev_end), s) != cudaSuccess) return TFA_ERR_CUDA;
   const int64_t G = a->num_q_heads / a->num_kv_heads;

@@ -53,8 +53,8 @@ struct FwdParams {
   const int* item_list;    // decode kernel: existing items (g * max_splits + split), longest
                            // first, built on the device for the call (NULL: slot order)
   const int* item_count;   // number of entries of item_list
-  int* group_cnt;          // decode kernel with splits: per work group, splits finished so far
-                           // (self-resetting); the last one merges the group's partials
+  int* group_cnt;          // decode kernel instance that merges in-kernel: per work group, splits
+                           // finished so far (self-resetting); the last one merges the group
 };
 
 // One unit of work: the packed q rows [row0, row0 + nrows) of kv head h of sequence b,
@@ -194,57 +194,6 @@ __device__ __forceinline__ GroupSrc resolve_group(const FwdParams& p, const Work
   s.slot = pos % p.block_size;
   s.page = p.num_blocks;
   if (s.valid > 0) s.page = __ldg(p.block_table + (int64_t)w.b * p.bt_s0 + pos / p.block_size);
-  return s;
-}
-
-// Block-table entries of one sequence held in a producer warp's registers: lane L holds
-// the physical block of page index base + L (cur) and base + 32 + L (nxt). The entries
-// of the pages ahead are requested up to 64 pages (at block_size 16, eight tiles) before
-// they are needed, so the table's latency (a DRAM round trip once L2 has been flushed)
-// overlaps the tiles in between instead of delaying every tile. Used when a tile has at
-// most 32 page groups (block_size >= 4); the shuffles are warp-collective.
-struct PageWindow {
-  const int* row;  // block_table row of the sequence
-  int npages;      // pages holding the sequence's kv_len tokens
-  int base;        // page index held by lane 0 in cur
-  int cur, nxt;
-};
-
-__device__ __forceinline__ int pw_load(const PageWindow& pw, int i) { return i < pw.npages ? __ldg(pw.row + i) : 0; }
-
-__device__ __forceinline__ void pw_start(PageWindow& pw, const FwdParams& p, const Work& w, int tile, int lane) {
-  pw.row = p.block_table + (int64_t)w.b * p.bt_s0;
-  pw.npages = (w.kv_len + p.block_size - 1) / p.block_size;
-  pw.base = (tile * kBN) / p.block_size;
-  pw.cur = pw_load(pw, pw.base + lane);
-  pw.nxt = pw_load(pw, pw.base + 32 + lane);
-}
-
-// Page group g of `tile` (lane g; every lane of the warp must call, lanes >= groups get
-// an unused result). Moves the window forward when the tile reaches past it; a tile's
-// pages always fit in one window (at most 32 of them for block_size >= 4).
-__device__ __forceinline__ GroupSrc pw_resolve(PageWindow& pw, const FwdParams& p, const Work& w, int tile, int g,
-                                               int lane) {
-  const int bs = p.block_size;
-  const int first = (tile * kBN) / bs;
-  const int last = (tile * kBN + kBN - 1) / bs;
-  if (last >= pw.base + 32) {  // warp-uniform: depends on the tile only
-    const int d = first - pw.base;  // 0 <= d <= 32 since tiles advance one at a time
-    const int src = (d + lane) & 31;
-    const int from_cur = __shfl_sync(0xffffffffu, pw.cur, src);
-    const int from_nxt = __shfl_sync(0xffffffffu, pw.nxt, src);
-    pw.cur = (d + lane < 32) ? from_cur : from_nxt;
-    pw.base = first;
-    pw.nxt = pw_load(pw, pw.base + 32 + lane);
-  }
-  const int R = p.box_rows;
-  const int pos = tile * kBN + g * R;
-  GroupSrc s;
-  const int valid = w.kv_len - pos;
-  s.valid = valid < 0 ? 0 : (valid > R ? R : valid);
-  s.slot = pos % bs;
-  const int pg = __shfl_sync(0xffffffffu, pw.cur, (pos / bs - pw.base) & 31);
-  s.page = s.valid > 0 ? pg : p.num_blocks;
   return s;
 }
 
@@ -413,20 +362,20 @@ __device__ __forceinline__ void producer_loop(const FwdParams& p, const KvMaps& 
 #endif
     if (w.tile_end == w.tile_begin) claim();
     if (lane_per_group) {
-      PageWindow pw;
-      if (w.tile_begin < w.tile_end) pw_start(pw, p, w, w.tile_begin, lane);
+      GroupSrc cur{}, nxt{};
+      if (lane < groups) cur = resolve_group(p, w, w.tile_begin, lane);
       for (int t = w.tile_begin; t < w.tile_end; ++t, ++c) {
-        if (t + 1 == w.tile_end) claim();
-        const GroupSrc src = pw_resolve(pw, p, w, t, lane, lane);
+        if (t + 1 < w.tile_end) {
+          if (lane < groups) nxt = resolve_group(p, w, t + 1, lane);
+        } else {
+          claim();
+        }
         const int st = c % STAGES;
         if (!mbar_wait(&empty[st], ((c / STAGES) & 1) ^ 1, abort_flag, p.err, kDevErrTimeoutProducer)) return;
         if (lane == 0) mbar_arrive_expect_tx(&full[st], KvStage<D>::kTensorBytes);
         __syncwarp();
-        if (lane < groups) issue_group_one<D>(p, maps, w, lane, src, 1, ring + st * KvStage<D>::kTensorBytes, &full[st], policy);
-#ifdef TFA_PROFILE
-        if (lane == 0 && p.rows_per_tile == 16) decode_tile_hook(c, 0);
-        if (lane == 0 && c == 0 && blockIdx.x == 0 && p.rows_per_tile == 16) decode_stamp_hook(3);
-#endif
+        if (lane < groups) issue_group_one<D>(p, maps, w, lane, cur, 1, ring + st * KvStage<D>::kTensorBytes, &full[st], policy);
+        cur = nxt;
       }
     } else {
       for (int t = w.tile_begin; t < w.tile_end; ++t, ++c) {
@@ -462,11 +411,12 @@ __device__ __forceinline__ void producer_follow_v(const FwdParams& p, const KvMa
     const int idx = item_slot[slot];
     if (idx >= p.num_items) return;
     const Work w = item_work[slot];
-    PageWindow pw;
-    if (lane_per_group && w.tile_begin < w.tile_end) pw_start(pw, p, w, w.tile_begin, lane);
+    GroupSrc cur{}, nxt{};
+    if (lane_per_group && lane < groups && w.tile_begin < w.tile_end) cur = resolve_group(p, w, w.tile_begin, lane);
     for (int t = w.tile_begin; t < w.tile_end; ++t, ++c) {
-      GroupSrc src{};
-      if (lane_per_group) src = pw_resolve(pw, p, w, t, lane, lane);
+      if (lane_per_group && lane < groups && t + 1 < w.tile_end) nxt = resolve_group(p, w, t + 1, lane);
+      const GroupSrc src = cur;
+      cur = nxt;
       const int st = c % STAGES;
       if (!mbar_wait(&empty[st], ((c / STAGES) & 1) ^ 1, abort_flag, p.err, kDevErrTimeoutProducer)) return;
       if (lane == 0) mbar_arrive_expect_tx(&full[st], KvStage<D>::kTensorBytes);
@@ -523,13 +473,8 @@ __device__ __forceinline__ void producer_loop_kv_slots(const FwdParams& p, const
       return;
     }
     if (w.tile_end == w.tile_begin) claim();
-    const bool lane_per_group = groups <= 32;
-    PageWindow pw;
-    if (lane_per_group && w.tile_begin < w.tile_end) pw_start(pw, p, w, w.tile_begin, lane);
     for (int t = w.tile_begin; t < w.tile_end; ++t) {
       if (t + 1 == w.tile_end) claim();
-      GroupSrc lsrc{};
-      if (lane_per_group) lsrc = pw_resolve(pw, p, w, t, lane, lane);
 #pragma unroll 1
       for (int which = 0; which < 2; ++which, ++c) {
         const int st = c % NSLOTS;
@@ -538,7 +483,7 @@ __device__ __forceinline__ void producer_loop_kv_slots(const FwdParams& p, const
         __syncwarp();
         const uint32_t base = smem_u32(slots + st * kSlotBytes);
         for (int g = lane; g < groups; g += 32) {
-          const GroupSrc src = lane_per_group ? lsrc : resolve_group(p, w, t, g);
+          const GroupSrc src = resolve_group(p, w, t, g);
           if (which == 0)
             issue_group_tensor<D>(p, &maps.k_box, &maps.k_row, w, src, base + g * p.box_rows * 128, &full[st], policy);
           else
@@ -593,7 +538,8 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 // Device-side launch helpers live in the per-kernel .cu files.
 template <int D>
-cudaError_t launch_decode(const FwdParams& p, const KvMaps& maps, const CUtensorMap& q_map, int grid, cudaStream_t s);
+cudaError_t launch_decode(const FwdParams& p, const KvMaps& maps, const CUtensorMap& q_map, int grid, cudaStream_t s,
+                          int mode);
 template <int D>
 cudaError_t launch_prefill(const FwdParams& p, const KvMaps& maps, int grid, cudaStream_t s);
 template <int D>

@@ -17,6 +17,7 @@
 // rows by TMA into a per-item-slot buffer, ahead of time: an item boundary then costs no
 // global-memory round trip on the consumer side.
 #include <cmath>
+#include <mutex>
 
 #include "tfa_common.cuh"
 
@@ -137,7 +138,11 @@ __device__ __forceinline__ void merge_splits(const FwdParams& p, const Work& w, 
   }
 }
 
-template <int D, bool kList>
+// kMode: 0 = items in slot order, split partials (if any) merged by the combine kernel;
+// 1 = items from the device-built list (the only instance that reads it), combine kernel;
+// 2 = items in slot order, split partials merged inside this kernel by the last split of
+// each group (the only instance that touches the per-group counters).
+template <int D, int kMode>
 __global__ void __launch_bounds__(224, 1)
     decode_kernel(const __grid_constant__ FwdParams p, const __grid_constant__ KvMaps maps,
                   const __grid_constant__ CUtensorMap q_map) {
@@ -165,7 +170,7 @@ __global__ void __launch_bounds__(224, 1)
   const int warp = tid >> 5;
   const int lane = tid & 31;
   if (tid == 0) STAMP(0);
-  if constexpr (!kList) {
+  if constexpr (kMode != 1) {
     // The first item of this CTA is item blockIdx.x: bring its sequence's lengths and the
     // start of its block-table row into L2 while the CTA sets up (the producer's first
     // loads then hit L2 instead of waiting a DRAM round trip after the prologue).
@@ -216,7 +221,7 @@ __global__ void __launch_bounds__(224, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    producer_loop<D, Cfg::kKSlots, kList>(p, maps, k_ring, full_k, empty_k, item_full, item_empty, item_slot, item_work, &q_map,
+    producer_loop<D, Cfg::kKSlots, kMode == 1>(p, maps, k_ring, full_k, empty_k, item_full, item_empty, item_slot, item_work, &q_map,
                                    q_smem, Cfg::kQBytes, q_full, &abort_flag, lane);
   } else if (warp == 6) {
     producer_follow_v<D, Cfg::kVSlots>(p, maps, v_ring, full_v, empty_v, item_full, item_empty, item_slot, item_work,
@@ -532,7 +537,7 @@ __global__ void __launch_bounds__(224, 1)
         }
         if (warp == 2 && lane == 0 && k == 0 && r == 0) STAMP(17);
       }
-      if (!direct) {
+      if (kMode == 2 && !direct) {
         // Split combine inside the kernel: every split publishes its rows, then counts
         // itself done for the group; the split that completes the count merges them all
         // (and resets the count for the next launch).
@@ -584,22 +589,23 @@ int decode_smem_bytes() {
 }
 
 template <int D>
-cudaError_t launch_decode(const FwdParams& p, const KvMaps& maps, const CUtensorMap& q_map, int grid, cudaStream_t s) {
-  static bool configured[128][2] = {};
+cudaError_t launch_decode(const FwdParams& p, const KvMaps& maps, const CUtensorMap& q_map, int grid, cudaStream_t s,
+                          int mode) {
+  static bool configured[128][3] = {};
+  static std::mutex mu;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
-  const int li = p.item_list != nullptr ? 1 : 0;  // the instance that reads the item list
-  if (!configured[dev][li]) {
-    cudaError_t e = cudaFuncSetAttribute(li ? decode_kernel<D, true> : decode_kernel<D, false>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, DecodeCfg<D>::kDynBytes);
-    if (e != cudaSuccess) return e;
-    configured[dev][li] = true;
+  if (dev < 0 || dev >= 128 || mode < 0 || mode > 2) return cudaErrorInvalidValue;
+  auto kernel = mode == 0 ? decode_kernel<D, 0> : mode == 1 ? decode_kernel<D, 1> : decode_kernel<D, 2>;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!configured[dev][mode]) {
+      cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DecodeCfg<D>::kDynBytes);
+      if (e != cudaSuccess) return e;
+      configured[dev][mode] = true;
+    }
   }
-  if (li)
-    decode_kernel<D, true><<<grid, 224, DecodeCfg<D>::kDynBytes, s>>>(p, maps, q_map);
-  else
-    decode_kernel<D, false><<<grid, 224, DecodeCfg<D>::kDynBytes, s>>>(p, maps, q_map);
+  kernel<<<grid, 224, DecodeCfg<D>::kDynBytes, s>>>(p, maps, q_map);
   return cudaGetLastError();
 }
 
@@ -618,8 +624,8 @@ extern "C" __attribute__((visibility("default"))) int tfa_decode_ends_read(unsig
 
 template int decode_smem_bytes<64>();
 template int decode_smem_bytes<128>();
-template cudaError_t launch_decode<64>(const FwdParams&, const KvMaps&, const CUtensorMap&, int, cudaStream_t);
-template cudaError_t launch_decode<128>(const FwdParams&, const KvMaps&, const CUtensorMap&, int,
-                                              cudaStream_t);
+template cudaError_t launch_decode<64>(const FwdParams&, const KvMaps&, const CUtensorMap&, int, cudaStream_t, int);
+template cudaError_t launch_decode<128>(const FwdParams&, const KvMaps&, const CUtensorMap&, int, cudaStream_t,
+                                        int);
 
 }  // namespace tfa

@@ -166,6 +166,10 @@ def flash_attn_varlen_func(
 # sm_100a path
 # ---------------------------------------------------------------------------
 _workspaces: dict[tuple[int, int], torch.Tensor] = {}
+# Workspaces replaced by a larger one stay allocated: a CUDA graph captured with an earlier
+# call (vLLM captures one per batch size) keeps using the old buffer's address on replay,
+# and freed memory could be handed to another tensor.
+_retired_workspaces: list[torch.Tensor] = []
 
 
 def _workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor:
@@ -174,6 +178,8 @@ def _workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor:
     key = (device.index if device.index is not None else torch.cuda.current_device(), stream)
     ws = _workspaces.get(key)
     if ws is None or ws.numel() < nbytes:
+        if ws is not None:
+            _retired_workspaces.append(ws)
         ws = torch.zeros(max(nbytes, 4096), dtype=torch.uint8, device=device)
         _workspaces[key] = ws
     return ws

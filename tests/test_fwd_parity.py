@@ -410,3 +410,28 @@ def test_decode_with_device_item_list():
     out, _ = assert_parity(case)
     out2, _ = run_cuda(case)
     assert torch.equal(out, out2)
+
+
+def test_graph_replay_after_workspace_growth():
+    """A CUDA graph captured with a small call keeps using that call's workspace; a later,
+    larger call on the same stream grows the workspace, and replaying the graph afterwards
+    must still give the right result (the old buffer stays allocated)."""
+    small = baseline_config("C2").to("cuda")  # 16 splits: uses the workspace's split buffers
+    big = baseline_config("C4").to("cuda")
+    out = torch.empty_like(small.q)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        faf.flash_attn_varlen_func(**small.kwargs(), out=out)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            faf.flash_attn_varlen_func(**small.kwargs(), out=out)
+        big_out = torch.empty_like(big.q)
+        faf.flash_attn_varlen_func(**big.kwargs(), out=big_out, num_splits=16)  # needs a larger workspace
+        out.zero_()
+        g.replay()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(s):
+        assert faf.read_device_error() == 0
+    ref, _ = oracle(baseline_config("C2"))
+    assert (out.cpu().float() - ref).abs().max().item() <= OUT_TOL
