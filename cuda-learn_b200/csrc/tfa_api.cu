@@ -1,6 +1,7 @@
 // C ABI of the paged attention forward (declared in include/tfa.h): argument checks,
 // split-KV planning, TMA descriptor encoding and kernel launches. Host code only.
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
@@ -29,16 +30,18 @@ size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 // device < 0 plans for a B200 (148 SMs) without touching the CUDA runtime.
 constexpr int kB200Sms = 148;
 
+// Per-device attribute caches are atomics: host threads driving different streams of one
+// device may call in concurrently (a racing first query just stores the same value twice).
 int sm_count(int device) {
-  static int cache[kMaxDevices] = {};
+  static std::atomic<int> cache[kMaxDevices] = {};
   if (device < 0) return kB200Sms;
   if (device >= kMaxDevices) return 0;
-  if (cache[device] == 0) {
-    int n = 0;
+  int n = cache[device].load(std::memory_order_relaxed);
+  if (n == 0) {
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return 0;
-    cache[device] = n;
+    cache[device].store(n, std::memory_order_relaxed);
   }
-  return cache[device];
+  return n;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -300,14 +303,14 @@ int encode_maps(const tfa_fwd_params* a, int box_rows, KvMaps* m) {
 }
 
 int check_device(int dev) {
-  static int cc_major[kMaxDevices] = {};
+  static std::atomic<int> cc_major[kMaxDevices] = {};
   if (dev < 0 || dev >= kMaxDevices) return TFA_ERR_DEVICE;
-  if (cc_major[dev] == 0) {
-    int major = 0;
+  int major = cc_major[dev].load(std::memory_order_relaxed);
+  if (major == 0) {
     if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return TFA_ERR_CUDA;
-    cc_major[dev] = major;
+    cc_major[dev].store(major, std::memory_order_relaxed);
   }
-  return cc_major[dev] == 10 ? TFA_OK : TFA_ERR_DEVICE;
+  return major == 10 ? TFA_OK : TFA_ERR_DEVICE;
 }
 
 }  // namespace

@@ -1,5 +1,6 @@
 // LSE combine of split-KV partial outputs, and the gather debug kernel.
 #include <cmath>
+#include <mutex>
 
 #include "tfa_common.cuh"
 
@@ -190,13 +191,17 @@ cudaError_t launch_gather(const FwdParams& p, const KvMaps& maps, int max_tiles,
                           void* k_out, void* v_out, cudaStream_t s) {
   const int smem = KvStage<D>::kBytes + 1024;
   static bool configured[128] = {};
+  static std::mutex mu;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
-  if (!configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gather_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    configured[dev] = true;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!configured[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(gather_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (e != cudaSuccess) return e;
+      configured[dev] = true;
+    }
   }
   dim3 grid(max_tiles, p.batch, p.hkv);
   gather_kernel<D><<<grid, 128, smem, s>>>(p, maps, kv_offsets, reinterpret_cast<__nv_bfloat16*>(k_out),

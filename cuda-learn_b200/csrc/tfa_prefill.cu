@@ -25,6 +25,7 @@
 // Warps (320 threads): 0 = TMA producer (K and V in separate slots), 1 = MMA issuer and
 // TMEM owner, 2-5 = softmax/epilogue of tile A, 6-9 = softmax/epilogue of tile B.
 #include <cmath>
+#include <mutex>
 
 #include "tfa_common.cuh"
 
@@ -498,14 +499,17 @@ int prefill_smem_bytes() {
 template <int D>
 cudaError_t launch_prefill(const FwdParams& p, const KvMaps& maps, int grid, cudaStream_t s) {
   static bool configured[128] = {};
+  static std::mutex mu;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
-  if (!configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(prefill_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         PrefillCfg<D>::kDynBytes);
-    if (e != cudaSuccess) return e;
-    configured[dev] = true;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!configured[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(prefill_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, PrefillCfg<D>::kDynBytes);
+      if (e != cudaSuccess) return e;
+      configured[dev] = true;
+    }
   }
   prefill_kernel<D><<<grid, 320, PrefillCfg<D>::kDynBytes, s>>>(p, maps);
   return cudaGetLastError();

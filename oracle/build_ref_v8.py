@@ -10,7 +10,7 @@ and ``helper.h`` in the reference tree); it is compiled as the reference itself 
 
 Usage (where the reference tree is mounted)::
 
-    python oracle/build_ref_v8.py /root/reference
+    python oracle/build_ref_v8.py <path of the reference tree>
 """
 
 from __future__ import annotations
@@ -56,8 +56,11 @@ def build(ref_root: str) -> Path:
     so = build_dir / f"{NAME}.so"
     dst = OUT / f"{NAME}.so"
     shutil.copy2(so, dst)
+    shutil.rmtree(build_dir, ignore_errors=True)  # objects only; the module is the copy above
     return dst
 
 
 if __name__ == "__main__":
-    print(build(sys.argv[1] if len(sys.argv) > 1 else "/root/reference"))
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: python oracle/build_ref_v8.py <path of the reference tree>")
+    print(build(sys.argv[1]))

@@ -2,7 +2,7 @@
 
 Run here (where the reference tree is mounted), never on the GPU box::
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py <path of the reference tree>
 
 The reference module ``flash_attention_backend/toy_flash_attn/flash_attention_func.py``
 cannot be imported in this container (it imports vLLM's FA2 CUDA extension and JIT-builds
@@ -134,4 +134,6 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: python tests/golden/make_golden.py <path of the reference tree>")
+    main(sys.argv[1])
