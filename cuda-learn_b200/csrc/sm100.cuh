@@ -68,6 +68,19 @@ __device__ __forceinline__ void prefetch_l2(const void* p) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(p)));
 }
 
+// Per-warpgroup register budget (setmaxnreg): every thread of the warpgroup executes it.
+// A decrease returns registers to the CTA's pool; an increase waits until the pool holds
+// enough, so the launch's registers (threads x registers per thread) must cover the sum of
+// the budgets (the launch code checks this before the kernel is started).
+template <uint32_t N>
+__device__ __forceinline__ void warpgroup_reg_release() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void warpgroup_reg_claim() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // Named barrier over a subset of the CTA's warps (id 0 is __syncthreads).
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
