@@ -3,12 +3,10 @@
 // One work item = (sequence b, kv head h, q tile pair of 2 x 128 packed rows, kv split).
 // A packed row is one (q token, q head of the GQA group) pair, so all rows of an item
 // share the kv head and every K/V tile is read once for the whole group. The two 128-row
-// tiles A and B each have their own softmax warpgroup, and the MMA warp interleaves them
-// so that one tile's softmax runs while the tensor core works on the other tile:
-//
-//   tensor core:  PV_A(j) QK_A(j+1) PV_B(j) QK_B(j+1) PV_A(j+1) ...
-//   softmax A:              [softmax A(j+1) ..........]
-//   softmax B:                                [softmax B(j+1) ..........]
+// tiles A and B each have their own softmax warpgroup; at D = 64 they also have their own
+// MMA warp, so the two chains QK(j+1) -> softmax(j+1) -> P.V(j+1) run independently, and at
+// D = 128 one MMA warp interleaves them (PV_A QK_A PV_B QK_B ...). Either way one tile's
+// softmax overlaps the other tile's tensor-core work.
 //
 // Per kv tile and q tile:
 //   S[128 x 128] = Q[128 x D] . K^T   (tcgen05, A = Q K-major, B = K K-major), S in TMEM
@@ -23,11 +21,13 @@
 // bf16/fp32 range), so most tiles need no O round trip.
 //
 // Warps (384 threads, three warpgroups): 0 = TMA producer (K and V in separate slots), 1 =
-// MMA issuer and TMEM owner, 2-3 = idle, 4-7 = softmax/epilogue of tile A, 8-11 =
-// softmax/epilogue of tile B. The first warpgroup gives up registers (setmaxnreg) so that
+// MMA issuer of tile A (both tiles at D = 128) and TMEM owner, 2 = MMA issuer of tile B at
+// D = 64 (idle at D = 128), 3 = idle, 4-7 =
+// softmax/epilogue of tile A, 8-11 = softmax/epilogue of tile B. The first warpgroup
+// gives up registers (setmaxnreg) so that
 // each softmax thread can hold its 128-score row without spilling: 384 threads launch
 // with 168 registers each (a sub-partition holds 3 warps x 32 x 168 of its 16 K
-// registers), then 56 for the producer/MMA warpgroup and 224 for the softmax ones.
+// registers), then 72 for the producer/MMA warpgroup and 216 for the softmax ones.
 #include <cmath>
 #include <mutex>
 
@@ -60,6 +60,9 @@ struct PrefillCfg {
   // overwrite S as soon as the softmax has loaded S(j), overlapping the softmax's exponent
   // phase. At D = 128 (2 x 128 S + 2 x 128 O = 512 columns) P aliases the first 64 S columns.
   static constexpr bool kSeparateP = (D == 64);
+  // MMA warps: one per q tile at D = 64 (each tile's chain then waits only on its own
+  // softmax: P2 265 -> 229 us per call), one for both tiles at D = 128.
+  static constexpr int kMmaWarps = (D == 64) ? 2 : 1;
 };
 
 __device__ __forceinline__ uint32_t s_col_of(int x) { return x == 0 ? 0u : 128u; }
@@ -71,8 +74,8 @@ __device__ __forceinline__ uint32_t p_col_of(int x) {
 
 constexpr int kThreads = 384;
 constexpr uint32_t kRegsLaunch = 168;   // per thread at launch
-constexpr uint32_t kRegsControl = 56;   // producer / MMA warpgroup after the split
-constexpr uint32_t kRegsSoftmax = 224;  // each softmax warpgroup after the split
+constexpr uint32_t kRegsControl = 72;   // producer / MMA warpgroup after the split
+constexpr uint32_t kRegsSoftmax = 216;  // each softmax warpgroup after the split
 static_assert(128 * kRegsControl + 256 * kRegsSoftmax <= kThreads * kRegsLaunch,
               "register split exceeds the launch's registers");
 
@@ -104,7 +107,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (tid == 0) {
     for (int i = 0; i < Cfg::kSlots; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 1);
+      mbar_init(&empty[i], Cfg::kMmaWarps);  // released by every MMA warp
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
@@ -113,7 +116,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&o_full[i], 1);
       mbar_init(&o_free[i], 4);
       mbar_init(&item_full[i], 1);
-      mbar_init(&item_empty[i], 9);
+      mbar_init(&item_empty[i], 8 + Cfg::kMmaWarps);  // MMA warps + 8 softmax warps
       mbar_init(&q_full[i], 8);
     }
     abort_flag = 0;
@@ -132,85 +135,233 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (tid == 0) allow_dependent_launch();
 
   if (warp < 4) {
-    // producer / MMA warpgroup: every warp gives up registers first (warps 2-3 then idle)
+    // producer / MMA warpgroup: every warp gives up registers first (warp 3 then idles)
     warpgroup_reg_release<kRegsControl>();
     if (warp == 0) {
       producer_loop_kv_slots<D, Cfg::kSlots>(p, maps, slots, full, empty, item_full, item_empty, item_slot,
                                              &abort_flag, lane);
-    } else if (warp == 1) {
-      // ------------------------------------------------------------ MMA issuer
-      const uint32_t idesc_qk = make_idesc_bf16_f32(128, 128, false, false);
-      const uint32_t idesc_pv = make_idesc_bf16_f32(128, D, false, true);
-      const uint32_t q_addr = smem_u32(q_smem);
-      int c = 0;           // slot loads consumed (2 per kv tile)
-      int ts0 = 0, ts1 = 0;  // kv tiles processed per q tile (phase counters)
-      int oi0 = 0, oi1 = 0;  // non-empty items per q tile
-      bool ok = true;
-      auto slot_wait = [&](int cc) -> bool {
-        return PROF_WAIT(0, mbar_wait(&full[cc % Cfg::kSlots], (cc / Cfg::kSlots) & 1, &abort_flag, p.err, kDevErrTimeoutMma));
-      };
-      auto issue_qk = [&](int x, int kslot) {
-        const uint32_t k_addr = smem_u32(slots + kslot * Cfg::kSlotBytes);
-        const uint32_t qx = q_addr + x * Cfg::kQBytes;
+    } else if (warp == 1 || (warp == 2 && Cfg::kMmaWarps == 2)) {
+      if constexpr (Cfg::kMmaWarps == 2) {
+        // ------------------------------------------------------------ MMA issuers
+        // One MMA warp per q tile (warp 1: tile A, warp 2: tile B), so each tile's chain
+        // QK(j+1) -> softmax -> P.V(j) waits only on its own softmax: a group of MMAs holds its
+        // issuing thread for about its execution time, and one warp serving both tiles in a
+        // fixed order made each tile's P.V wait behind the other tile's QK and P.V. A K/V slot
+        // is released once both warps are done with it (empty barriers count two).
+        const int x = warp - 1;
+        const uint32_t idesc_qk = make_idesc_bf16_f32(128, 128, false, false);
+        const uint32_t idesc_pv = make_idesc_bf16_f32(128, D, false, true);
+        const uint32_t qx = smem_u32(q_smem) + x * Cfg::kQBytes;
+        int c = 0;   // slot loads consumed (2 per kv tile)
+        int ts = 0;  // kv tiles processed by this q tile (phase counter)
+        int oi = 0;  // items with rows in this q tile
+        bool ok = true;
+        auto slot_wait = [&](int cc) -> bool {
+          return PROF_WAIT(0, mbar_wait(&full[cc % Cfg::kSlots], (cc / Cfg::kSlots) & 1, &abort_flag, p.err, kDevErrTimeoutMma));
+        };
+        auto issue_qk = [&](int kslot) {
+          const uint32_t k_addr = smem_u32(slots + kslot * Cfg::kSlotBytes);
   #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * KvStage<D>::kPanelBytes + (kk & 3) * 32;
-          umma_bf16_ss(tmem + s_col_of(x), make_sdesc_sw128(qx + off, 16, 1024),
-                       make_sdesc_sw128(k_addr + off, 16, 1024), idesc_qk, kk > 0 ? 1u : 0u);
-        }
-        umma_commit(&s_full[x]);
-      };
-      auto issue_pv = [&](int x, int vslot, bool first) {
-        const uint32_t v_addr = smem_u32(slots + vslot * Cfg::kSlotBytes);
-        const uint32_t p_tmem = tmem + p_col_of<D>(x);  // P as bf16 pairs (over S's first 64 columns at D = 128)
-  #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          umma_bf16_ts(tmem + o_col_of(x), p_tmem + kk * 8,
-                       make_sdesc_sw128(v_addr + kk * 2048, KvStage<D>::kPanelBytes, 1024), idesc_pv,
-                       (!first || kk > 0) ? 1u : 0u);
-        }
-        umma_commit(&o_full[x]);
-      };
-      for (int k = 0; ok; ++k) {
-        const int slot = k & 1;
-        if (!PROF_WAIT(3, mbar_wait(&item_full[slot], (k >> 1) & 1, &abort_flag, p.err, kDevErrTimeoutMma))) break;
-        const int idx = item_slot[slot];
-        if (idx >= p.num_items) break;
-        const Work w = get_work(p, idx);
-        // Test hook (FwdParams::debug_stall): wait for a phase that never completes, so the
-        // time limit expires, the error word is set and every warp of the CTA unwinds.
-        if (p.debug_stall && k == 0 && !mbar_wait(&stall_bar, 0, &abort_flag, p.err, kDevErrTimeoutMma)) break;
-        const int n = w.tile_end - w.tile_begin;
-        const int nx = w.nrows > kRows ? 2 : 1;  // q tiles with rows
-        if (!PROF_WAIT(3, mbar_wait(&q_full[slot], (k >> 1) & 1, &abort_flag, p.err, kDevErrTimeoutMma))) break;
-        if (lane == 0 && n > 0) {
-          // QK of the first kv tile for both q tiles
-          ok = slot_wait(c);
-          if (ok) {
-            tc_fence_after();
-            for (int x = 0; x < nx; ++x) issue_qk(x, c % Cfg::kSlots);
-            umma_commit(&empty[c % Cfg::kSlots]);  // K_0 consumed
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * KvStage<D>::kPanelBytes + (kk & 3) * 32;
+            umma_bf16_ss(tmem + s_col_of(x), make_sdesc_sw128(qx + off, 16, 1024),
+                         make_sdesc_sw128(k_addr + off, 16, 1024), idesc_qk, kk > 0 ? 1u : 0u);
           }
-          for (int j = 0; ok && j < n; ++j) {
-            const int kc = c + 2 * j;  // slot load index of K_j; V_j is kc + 1
-            const bool more = j + 1 < n;
-            if constexpr (Cfg::kSeparateP) {
-              // QK(j+1) as soon as the softmax has loaded S(j) (P lives elsewhere), then P.V(j)
-              if (more) {
-                if (!slot_wait(kc + 2)) {  // K_{j+1}
-                  ok = false;
-                  break;
-                }
-                for (int x = 0; x < nx; ++x) {
-                  if (!PROF_WAIT(2, mbar_wait(&s_free[x], (x ? ts1 : ts0) & 1, &abort_flag, p.err, kDevErrTimeoutMma))) {
+          umma_commit(&s_full[x]);
+        };
+        auto issue_pv = [&](int vslot, bool first) {
+          const uint32_t v_addr = smem_u32(slots + vslot * Cfg::kSlotBytes);
+          const uint32_t p_tmem = tmem + p_col_of<D>(x);  // P as bf16 pairs (over S's first 64 columns at D = 128)
+  #pragma unroll
+          for (int kk = 0; kk < kBN / 16; ++kk) {
+            umma_bf16_ts(tmem + o_col_of(x), p_tmem + kk * 8,
+                         make_sdesc_sw128(v_addr + kk * 2048, KvStage<D>::kPanelBytes, 1024), idesc_pv,
+                         (!first || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&o_full[x]);
+        };
+        // A slot this q tile does not read (an item without rows in it): released once filled.
+        auto pass_slot = [&](int cc) -> bool {
+          if (!slot_wait(cc)) return false;
+          mbar_arrive(&empty[cc % Cfg::kSlots]);
+          return true;
+        };
+        for (int k = 0; ok; ++k) {
+          const int slot = k & 1;
+          if (!PROF_WAIT(3, mbar_wait(&item_full[slot], (k >> 1) & 1, &abort_flag, p.err, kDevErrTimeoutMma))) break;
+          const int idx = item_slot[slot];
+          if (idx >= p.num_items) break;
+          const Work w = get_work(p, idx);
+          // Test hook (FwdParams::debug_stall): wait for a phase that never completes, so the
+          // time limit expires, the error word is set and every warp of the CTA unwinds.
+          if (p.debug_stall && k == 0 && !mbar_wait(&stall_bar, 0, &abort_flag, p.err, kDevErrTimeoutMma)) break;
+          const int n = w.tile_end - w.tile_begin;
+          const bool active = (x == 0) || (w.nrows > kRows);  // this q tile has rows
+          if (!PROF_WAIT(3, mbar_wait(&q_full[slot], (k >> 1) & 1, &abort_flag, p.err, kDevErrTimeoutMma))) break;
+          if (lane == 0 && n > 0) {
+            if (!active) {
+              for (int j = 0; ok && j < 2 * n; ++j) ok = pass_slot(c + j);
+            } else {
+              ok = slot_wait(c);  // K_0
+              if (ok) {
+                tc_fence_after();
+                issue_qk(c % Cfg::kSlots);
+                umma_commit(&empty[c % Cfg::kSlots]);
+              }
+              for (int j = 0; ok && j < n; ++j) {
+                const int kc = c + 2 * j;  // slot load index of K_j; V_j is kc + 1
+                const bool more = j + 1 < n;
+                if constexpr (Cfg::kSeparateP) {
+                  // QK(j+1) as soon as the softmax has loaded S(j) (P lives elsewhere), then P.V(j)
+                  if (more) {
+                    if (!slot_wait(kc + 2) ||
+                        !PROF_WAIT(2, mbar_wait(&s_free[x], ts & 1, &abort_flag, p.err, kDevErrTimeoutMma))) {
+                      ok = false;
+                      break;
+                    }
+                    tc_fence_after();
+                    issue_qk((kc + 2) % Cfg::kSlots);
+                    umma_commit(&empty[(kc + 2) % Cfg::kSlots]);  // K_{j+1} consumed
+                  }
+                  if (!slot_wait(kc + 1) ||  // V_j
+                      !PROF_WAIT(1, mbar_wait(&p_full[x], ts & 1, &abort_flag, p.err, kDevErrTimeoutMma)) ||
+                      (j == 0 && !PROF_WAIT(2, mbar_wait(&o_free[x], (oi & 1) ^ 1, &abort_flag, p.err, kDevErrTimeoutMma)))) {
                     ok = false;
                     break;
                   }
                   tc_fence_after();
-                  issue_qk(x, (kc + 2) % Cfg::kSlots);
+                  issue_pv((kc + 1) % Cfg::kSlots, j == 0);
+                  umma_commit(&empty[(kc + 1) % Cfg::kSlots]);  // V_j consumed
+                  ++ts;
+                } else {
+                  // P(j) overwrites the first columns of S(j): QK(j+1) waits until P.V(j) has read it
+                  if (!slot_wait(kc + 1) ||  // V_j
+                      !PROF_WAIT(1, mbar_wait(&p_full[x], ts & 1, &abort_flag, p.err, kDevErrTimeoutMma)) ||
+                      (j == 0 && !PROF_WAIT(2, mbar_wait(&o_free[x], (oi & 1) ^ 1, &abort_flag, p.err, kDevErrTimeoutMma)))) {
+                    ok = false;
+                    break;
+                  }
+                  tc_fence_after();
+                  issue_pv((kc + 1) % Cfg::kSlots, j == 0);
+                  umma_commit(&empty[(kc + 1) % Cfg::kSlots]);  // V_j consumed
+                  ++ts;
+                  if (more) {
+                    if (!mbar_wait(&o_full[x], (ts - 1) & 1, &abort_flag, p.err, kDevErrTimeoutMma) || !slot_wait(kc + 2)) {
+                      ok = false;
+                      break;
+                    }
+                    tc_fence_after();
+                    issue_qk((kc + 2) % Cfg::kSlots);
+                    umma_commit(&empty[(kc + 2) % Cfg::kSlots]);  // K_{j+1} consumed
+                  }
+                }
+              }
+            }
+          }
+          ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+          ts = __shfl_sync(0xffffffffu, ts, 0);
+          if (n > 0 && active) ++oi;
+          c += 2 * n;
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&item_empty[slot]);
+        }
+      } else {
+        // ------------------------------------------------------------ MMA issuer (both tiles)
+        // At D = 128 one warp issues for both tiles in the order PV_A(j) QK_A(j+1) PV_B(j)
+        // QK_B(j+1): the tiles' large MMA groups then alternate on the tensor pipe instead
+        // of colliding (two MMA warps measured 17 % slower on P1).
+        // ------------------------------------------------------------ MMA issuer
+        const uint32_t idesc_qk = make_idesc_bf16_f32(128, 128, false, false);
+        const uint32_t idesc_pv = make_idesc_bf16_f32(128, D, false, true);
+        const uint32_t q_addr = smem_u32(q_smem);
+        int c = 0;           // slot loads consumed (2 per kv tile)
+        int ts0 = 0, ts1 = 0;  // kv tiles processed per q tile (phase counters)
+        int oi0 = 0, oi1 = 0;  // non-empty items per q tile
+        bool ok = true;
+        auto slot_wait = [&](int cc) -> bool {
+          return PROF_WAIT(0, mbar_wait(&full[cc % Cfg::kSlots], (cc / Cfg::kSlots) & 1, &abort_flag, p.err, kDevErrTimeoutMma));
+        };
+        auto issue_qk = [&](int x, int kslot) {
+          const uint32_t k_addr = smem_u32(slots + kslot * Cfg::kSlotBytes);
+          const uint32_t qx = q_addr + x * Cfg::kQBytes;
+    #pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * KvStage<D>::kPanelBytes + (kk & 3) * 32;
+            umma_bf16_ss(tmem + s_col_of(x), make_sdesc_sw128(qx + off, 16, 1024),
+                         make_sdesc_sw128(k_addr + off, 16, 1024), idesc_qk, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[x]);
+        };
+        auto issue_pv = [&](int x, int vslot, bool first) {
+          const uint32_t v_addr = smem_u32(slots + vslot * Cfg::kSlotBytes);
+          const uint32_t p_tmem = tmem + p_col_of<D>(x);  // P as bf16 pairs (over S's first 64 columns at D = 128)
+    #pragma unroll
+          for (int kk = 0; kk < kBN / 16; ++kk) {
+            umma_bf16_ts(tmem + o_col_of(x), p_tmem + kk * 8,
+                         make_sdesc_sw128(v_addr + kk * 2048, KvStage<D>::kPanelBytes, 1024), idesc_pv,
+                         (!first || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&o_full[x]);
+        };
+        for (int k = 0; ok; ++k) {
+          const int slot = k & 1;
+          if (!PROF_WAIT(3, mbar_wait(&item_full[slot], (k >> 1) & 1, &abort_flag, p.err, kDevErrTimeoutMma))) break;
+          const int idx = item_slot[slot];
+          if (idx >= p.num_items) break;
+          const Work w = get_work(p, idx);
+          // Test hook (FwdParams::debug_stall): wait for a phase that never completes, so the
+          // time limit expires, the error word is set and every warp of the CTA unwinds.
+          if (p.debug_stall && k == 0 && !mbar_wait(&stall_bar, 0, &abort_flag, p.err, kDevErrTimeoutMma)) break;
+          const int n = w.tile_end - w.tile_begin;
+          const int nx = w.nrows > kRows ? 2 : 1;  // q tiles with rows
+          if (!PROF_WAIT(3, mbar_wait(&q_full[slot], (k >> 1) & 1, &abort_flag, p.err, kDevErrTimeoutMma))) break;
+          if (lane == 0 && n > 0) {
+            // QK of the first kv tile for both q tiles
+            ok = slot_wait(c);
+            if (ok) {
+              tc_fence_after();
+              for (int x = 0; x < nx; ++x) issue_qk(x, c % Cfg::kSlots);
+              umma_commit(&empty[c % Cfg::kSlots]);  // K_0 consumed
+            }
+            for (int j = 0; ok && j < n; ++j) {
+              const int kc = c + 2 * j;  // slot load index of K_j; V_j is kc + 1
+              const bool more = j + 1 < n;
+              if constexpr (Cfg::kSeparateP) {
+                // QK(j+1) as soon as the softmax has loaded S(j) (P lives elsewhere), then P.V(j)
+                if (more) {
+                  if (!slot_wait(kc + 2)) {  // K_{j+1}
+                    ok = false;
+                    break;
+                  }
+                  for (int x = 0; x < nx; ++x) {
+                    if (!PROF_WAIT(2, mbar_wait(&s_free[x], (x ? ts1 : ts0) & 1, &abort_flag, p.err, kDevErrTimeoutMma))) {
+                      ok = false;
+                      break;
+                    }
+                    tc_fence_after();
+                    issue_qk(x, (kc + 2) % Cfg::kSlots);
+                  }
+                  if (!ok) break;
+                  umma_commit(&empty[(kc + 2) % Cfg::kSlots]);  // K_{j+1} consumed
+                }
+                if (!slot_wait(kc + 1)) {  // V_j
+                  ok = false;
+                  break;
+                }
+                for (int x = 0; x < nx; ++x) {
+                  const int tsx = x ? ts1 : ts0, oix = x ? oi1 : oi0;
+                  if (!PROF_WAIT(1, mbar_wait(&p_full[x], tsx & 1, &abort_flag, p.err, kDevErrTimeoutMma)) ||
+                      (j == 0 && !PROF_WAIT(2, mbar_wait(&o_free[x], (oix & 1) ^ 1, &abort_flag, p.err, kDevErrTimeoutMma)))) {
+                    ok = false;
+                    break;
+                  }
+                  tc_fence_after();
+                  issue_pv(x, (kc + 1) % Cfg::kSlots, j == 0);
+                  if (x) ++ts1; else ++ts0;
                 }
                 if (!ok) break;
-                umma_commit(&empty[(kc + 2) % Cfg::kSlots]);  // K_{j+1} consumed
+                umma_commit(&empty[(kc + 1) % Cfg::kSlots]);  // V_j consumed
+                continue;
               }
               if (!slot_wait(kc + 1)) {  // V_j
                 ok = false;
@@ -226,53 +377,35 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_after();
                 issue_pv(x, (kc + 1) % Cfg::kSlots, j == 0);
                 if (x) ++ts1; else ++ts0;
+                if (more) {
+                  // QK(j+1) overwrites S, whose first columns hold the P this P.V reads:
+                  // wait for the P.V to finish. K_{j+1} is awaited only now, so its load
+                  // overlaps the softmax of tile A.
+                  if (!mbar_wait(&o_full[x], ((x ? ts1 : ts0) - 1) & 1, &abort_flag, p.err, kDevErrTimeoutMma) ||
+                      (x == 0 && !slot_wait(kc + 2))) {
+                    ok = false;
+                    break;
+                  }
+                  tc_fence_after();
+                  issue_qk(x, (kc + 2) % Cfg::kSlots);
+                }
               }
               if (!ok) break;
-              umma_commit(&empty[(kc + 1) % Cfg::kSlots]);  // V_j consumed
-              continue;
+              umma_commit(&empty[(kc + 1) % Cfg::kSlots]);            // V_j consumed
+              if (more) umma_commit(&empty[(kc + 2) % Cfg::kSlots]);  // K_{j+1} consumed
             }
-            if (!slot_wait(kc + 1)) {  // V_j
-              ok = false;
-              break;
-            }
-            for (int x = 0; x < nx; ++x) {
-              const int tsx = x ? ts1 : ts0, oix = x ? oi1 : oi0;
-              if (!PROF_WAIT(1, mbar_wait(&p_full[x], tsx & 1, &abort_flag, p.err, kDevErrTimeoutMma)) ||
-                  (j == 0 && !PROF_WAIT(2, mbar_wait(&o_free[x], (oix & 1) ^ 1, &abort_flag, p.err, kDevErrTimeoutMma)))) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-              issue_pv(x, (kc + 1) % Cfg::kSlots, j == 0);
-              if (x) ++ts1; else ++ts0;
-              if (more) {
-                // QK(j+1) overwrites S, whose first columns hold the P this P.V reads:
-                // wait for the P.V to finish. K_{j+1} is awaited only now, so its load
-                // overlaps the softmax of tile A.
-                if (!mbar_wait(&o_full[x], ((x ? ts1 : ts0) - 1) & 1, &abort_flag, p.err, kDevErrTimeoutMma) ||
-                    (x == 0 && !slot_wait(kc + 2))) {
-                  ok = false;
-                  break;
-                }
-                tc_fence_after();
-                issue_qk(x, (kc + 2) % Cfg::kSlots);
-              }
-            }
-            if (!ok) break;
-            umma_commit(&empty[(kc + 1) % Cfg::kSlots]);            // V_j consumed
-            if (more) umma_commit(&empty[(kc + 2) % Cfg::kSlots]);  // K_{j+1} consumed
           }
+          ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+          ts0 = __shfl_sync(0xffffffffu, ts0, 0);
+          ts1 = __shfl_sync(0xffffffffu, ts1, 0);
+          if (n > 0) {
+            ++oi0;
+            if (nx == 2) ++oi1;
+          }
+          c += 2 * n;
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&item_empty[slot]);
         }
-        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-        ts0 = __shfl_sync(0xffffffffu, ts0, 0);
-        ts1 = __shfl_sync(0xffffffffu, ts1, 0);
-        if (n > 0) {
-          ++oi0;
-          if (nx == 2) ++oi1;
-        }
-        c += 2 * n;
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&item_empty[slot]);
       }
     }
   } else {
