@@ -440,7 +440,7 @@ __device__ __forceinline__ void producer_follow_v(const FwdParams& p, const KvMa
 // Producer variant with separate K and V slots: tile t's K goes to slot (2u) % NSLOTS and
 // its V to slot (2u + 1) % NSLOTS, u counting tiles, each slot KvStage<D>::kTensorBytes.
 // Used by the prefill kernel, which keeps K_t and V_t alive for different lengths of time.
-template <int D, int NSLOTS>
+template <int D, int NSLOTS, bool kKOnly = false>
 __device__ __forceinline__ void producer_loop_kv_slots(const FwdParams& p, const KvMaps& maps, uint8_t* slots,
                                                        uint64_t* full, uint64_t* empty, uint64_t* item_full,
                                                        uint64_t* item_empty, int* item_slot,
@@ -477,6 +477,7 @@ __device__ __forceinline__ void producer_loop_kv_slots(const FwdParams& p, const
       if (t + 1 == w.tile_end) claim();
 #pragma unroll 1
       for (int which = 0; which < 2; ++which, ++c) {
+        if (kKOnly && which == 1) continue;  // the follower warp loads V into the odd slots
         const int st = c % NSLOTS;
         if (!mbar_wait(&empty[st], ((c / NSLOTS) & 1) ^ 1, abort_flag, p.err, kDevErrTimeoutProducer)) return;
         if (lane == 0) mbar_arrive_expect_tx(&full[st], kSlotBytes);
@@ -491,6 +492,39 @@ __device__ __forceinline__ void producer_loop_kv_slots(const FwdParams& p, const
         }
       }
     }
+  }
+}
+
+// Second producer warp of the prefill kernel: follows the item queue like a consumer and
+// issues the V loads of every kv tile (slot 2u + 1 for tile u) while producer_loop_kv_slots
+// (with kKOnly) issues the K loads, so two warps share the TMA issue work of a tile.
+template <int D, int NSLOTS>
+__device__ __forceinline__ void producer_follow_kv_slots(const FwdParams& p, const KvMaps& maps, uint8_t* slots,
+                                                         uint64_t* full, uint64_t* empty, uint64_t* item_full,
+                                                         uint64_t* item_empty, const int* item_slot,
+                                                         volatile int* abort_flag, int lane) {
+  constexpr int kSlotBytes = KvStage<D>::kTensorBytes;
+  const uint64_t policy = l2_policy_evict_first();
+  const int groups = kBN / p.box_rows;
+  int c = 1;  // slot load index of the next V
+  for (int k = 0;; ++k) {
+    const int slot = k & 1;
+    if (!mbar_wait(&item_full[slot], (k >> 1) & 1, abort_flag, p.err, kDevErrTimeoutProducer)) return;
+    const int idx = item_slot[slot];
+    if (idx >= p.num_items) return;
+    const Work w = get_work(p, idx);
+    for (int t = w.tile_begin; t < w.tile_end; ++t, c += 2) {
+      const int st = c % NSLOTS;
+      if (!mbar_wait(&empty[st], ((c / NSLOTS) & 1) ^ 1, abort_flag, p.err, kDevErrTimeoutProducer)) return;
+      if (lane == 0) mbar_arrive_expect_tx(&full[st], kSlotBytes);
+      __syncwarp();
+      const uint32_t base = smem_u32(slots + st * kSlotBytes);
+      for (int g = lane; g < groups; g += 32)
+        issue_group_tensor<D>(p, &maps.v_box, &maps.v_row, w, resolve_group(p, w, t, g), base + g * p.box_rows * 128,
+                              &full[st], policy);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&item_empty[slot]);
   }
 }
 

@@ -20,14 +20,14 @@
 // than 2^8 over the max its P values are referenced to (values of P stay <= 256, far inside
 // bf16/fp32 range), so most tiles need no O round trip.
 //
-// Warps (384 threads, three warpgroups): 0 = TMA producer (K and V in separate slots), 1 =
-// MMA issuer of tile A (both tiles at D = 128) and TMEM owner, 2 = MMA issuer of tile B at
-// D = 64 (idle at D = 128), 3 = idle, 4-7 =
-// softmax/epilogue of tile A, 8-11 = softmax/epilogue of tile B. The first warpgroup
-// gives up registers (setmaxnreg) so that
-// each softmax thread can hold its 128-score row without spilling: 384 threads launch
-// with 168 registers each (a sub-partition holds 3 warps x 32 x 168 of its 16 K
-// registers), then 72 for the producer/MMA warpgroup and 216 for the softmax ones.
+// Warps (384 threads, three warpgroups): 0 = TMA producer of K and item scheduler, 3 = TMA
+// producer of V (K and V tiles in separate, alternating slots), 1 = MMA issuer of tile A
+// (of both tiles at D = 128) and TMEM owner, 2 = MMA issuer of tile B at D = 64 (idle at
+// D = 128), 4-7 = softmax/epilogue of tile A, 8-11 = softmax/epilogue of tile B. The first
+// warpgroup gives up registers (setmaxnreg) so that each softmax thread can hold its
+// 128-score row without spilling: 384 threads launch with 168 registers each (a
+// sub-partition holds 3 warps x 32 x 168 of its 16 K registers), then 72 for the
+// producer/MMA warpgroup and 216 for the softmax ones.
 #include <cmath>
 #include <mutex>
 
@@ -116,7 +116,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&o_full[i], 1);
       mbar_init(&o_free[i], 4);
       mbar_init(&item_full[i], 1);
-      mbar_init(&item_empty[i], 8 + Cfg::kMmaWarps);  // MMA warps + 8 softmax warps
+      mbar_init(&item_empty[i], 9 + Cfg::kMmaWarps);  // MMA warps, 8 softmax warps, the V producer
       mbar_init(&q_full[i], 8);
     }
     abort_flag = 0;
@@ -135,11 +135,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (tid == 0) allow_dependent_launch();
 
   if (warp < 4) {
-    // producer / MMA warpgroup: every warp gives up registers first (warp 3 then idles)
+    // producer / MMA warpgroup: every warp gives up registers first
     warpgroup_reg_release<kRegsControl>();
     if (warp == 0) {
-      producer_loop_kv_slots<D, Cfg::kSlots>(p, maps, slots, full, empty, item_full, item_empty, item_slot,
-                                             &abort_flag, lane);
+      producer_loop_kv_slots<D, Cfg::kSlots, true>(p, maps, slots, full, empty, item_full, item_empty, item_slot,
+                                                   &abort_flag, lane);
+    } else if (warp == 3) {
+      producer_follow_kv_slots<D, Cfg::kSlots>(p, maps, slots, full, empty, item_full, item_empty, item_slot,
+                                               &abort_flag, lane);
     } else if (warp == 1 || (warp == 2 && Cfg::kMmaWarps == 2)) {
       if constexpr (Cfg::kMmaWarps == 2) {
         // ------------------------------------------------------------ MMA issuers
@@ -626,7 +629,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < 5; ++i) g_prefill_prof[base_idx + i] = prof[i];
   }
 #endif
-  if (abort_flag && warp == 0) {
+  if (abort_flag && (warp == 0 || warp == 3)) {
     const uint64_t t0 = global_timer_ns();
     while (global_timer_ns() - t0 < 100000ull) __nanosleep(1000);
   }
