@@ -38,6 +38,12 @@ namespace tfa {
 namespace {
 
 #ifdef TFA_PROFILE
+__device__ unsigned long long g_prefill_tl[2][16][12];
+#define TL(x, j, e) do { if (blockIdx.x == 0 && (j) < 16) g_prefill_tl[x][j][e] = global_timer_ns(); } while (0)
+#else
+#define TL(x, j, e) do {} while (0)
+#endif
+#ifdef TFA_PROFILE
 __device__ unsigned long long g_prefill_prof[1024 * 16];
 #define PROF_WAIT(cat, expr) ([&]() { const long long _t0 = clock64(); const bool _r = (expr); prof[cat] += clock64() - _t0; return _r; }())
 #else
@@ -163,6 +169,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           return PROF_WAIT(0, mbar_wait(&full[cc % Cfg::kSlots], (cc / Cfg::kSlots) & 1, &abort_flag, p.err, kDevErrTimeoutMma));
         };
         auto issue_qk = [&](int kslot) {
+          TL(x, ts, 0);
           const uint32_t k_addr = smem_u32(slots + kslot * Cfg::kSlotBytes);
   #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
@@ -171,8 +178,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                          make_sdesc_sw128(k_addr + off, 16, 1024), idesc_qk, kk > 0 ? 1u : 0u);
           }
           umma_commit(&s_full[x]);
+          TL(x, ts, 1);
         };
         auto issue_pv = [&](int vslot, bool first) {
+          TL(x, ts, 2);
           const uint32_t v_addr = smem_u32(slots + vslot * Cfg::kSlotBytes);
           const uint32_t p_tmem = tmem + p_col_of<D>(x);  // P as bf16 pairs (over S's first 64 columns at D = 128)
   #pragma unroll
@@ -182,6 +191,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                          (!first || kk > 0) ? 1u : 0u);
           }
           umma_commit(&o_full[x]);
+          TL(x, ts, 3);
         };
         // A slot this q tile does not read (an item without rows in it): released once filled.
         auto pass_slot = [&](int cc) -> bool {
@@ -467,11 +477,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
+          if (quad == 0 && lane == 0) TL(x, ts, 4);
           const int base = (w.tile_begin + j) * kBN;
           const bool full_tile = __all_sync(0xffffffffu, (base >= lo) && (base + kBN - 1 <= hi));
           // the whole 128-score row in registers, one TMEM load
           float sv[128];
           tmem_ld128_sync(s_col, sv);
+          if (quad == 0 && lane == 0) TL(x, ts, 5);
           if constexpr (Cfg::kSeparateP) {  // S(j) is in registers: QK(j+1) may overwrite it
             tc_fence_before();
             __syncwarp();
@@ -489,6 +501,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 64; ++i) m8[i & 7] = fmax3(m8[i & 7], sv[2 * i], sv[2 * i + 1]);
           float tmax = fmaxf(fmax3(m8[0], m8[1], m8[2]), fmax3(fmax3(m8[3], m8[4], m8[5]), m8[6], m8[7]));
           tmax *= p.scale_log2;
+          if (quad == 0 && lane == 0) TL(x, ts, 6);
           // reference max: moves only when the new max exceeds it by the threshold
           float alpha = 1.f;
           bool rescale = false;
@@ -545,9 +558,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               pk[c] = __uint_as_float(*reinterpret_cast<uint32_t*>(&h2));
             }
             if (h == 0 && p_wait) {
+              if (quad == 0 && lane == 0) TL(x, ts, 7);
               if (!mbar_wait(&o_full[x], (ts - 1) & 1, &abort_flag, p.err, kDevErrTimeoutSoftmax)) ok = false;
               tc_fence_after();
               p_wait = false;
+              if (quad == 0 && lane == 0) TL(x, ts, 8);
             }
             tmem_st32(p_col + h * 32, pk);
           }
@@ -557,6 +572,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           f2_unpack(rs2[0], r0, r1);
           f2_unpack(rs2[1], r2, r3);
           l += (r0 + r1) + (r2 + r3);
+          if (quad == 0 && lane == 0) TL(x, ts, 9);
           ++ts;
           tc_fence_before();
           __syncwarp();
@@ -674,6 +690,9 @@ cudaError_t launch_prefill(const FwdParams& p, const KvMaps& maps, int grid, cud
 }
 
 #ifdef TFA_PROFILE
+extern "C" __attribute__((visibility("default"))) int tfa_prefill_tl_read(unsigned long long* host) {
+  return (int)cudaMemcpyFromSymbol(host, g_prefill_tl, sizeof(g_prefill_tl));
+}
 extern "C" __attribute__((visibility("default"))) int tfa_prefill_prof_read(unsigned long long* host) {
   return (int)cudaMemcpyFromSymbol(host, g_prefill_prof, sizeof(g_prefill_prof));
 }
