@@ -53,7 +53,29 @@ def parse_args():
     ap.add_argument("--batch", type=int, default=None, help="override C5 batch (debug only)")
     ap.add_argument("--num-blocks", type=int, default=None, help="override C5 pool size (debug only)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="target CPU baseline sample time")
+    ap.add_argument("--profile-configs", default=None,
+                    help="comma-separated configurations (C1..C5, P1, P2) to run --calls times each through "
+                         "flash_attn_varlen_with_block_cu_bf16 and exit (a driver for ncu captures; no timing)")
+    ap.add_argument("--calls", type=int, default=3)
     return ap.parse_args()
+
+
+def run_profile_configs(args):
+    from toy_flash_attn import flash_attention_func as faf
+    from toy_flash_attn.workloads import baseline_config
+
+    torch.cuda.set_device(0)
+    for name in args.profile_configs.split(","):
+        case = baseline_config(name, device="cuda")
+        out = torch.empty_like(case.q)
+        for _ in range(args.calls):
+            call(case, out)
+        torch.cuda.synchronize()
+        if faf.read_device_error() != 0:
+            raise SystemExit(f"{name}: kernel reported an error")
+        print(f"ran {name} x{args.calls}", flush=True)
+        del case, out
+        torch.cuda.empty_cache()
 
 
 def peaks() -> dict:
@@ -700,7 +722,9 @@ def run_ours(args):
 
 def main():
     args = parse_args()
-    if args.impl == "reference":
+    if args.profile_configs:
+        run_profile_configs(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
