@@ -428,6 +428,38 @@ def time_graph_loop(case, seconds: float = 0.6) -> float:
     return e0.elapsed_time(e1) / n * 1e3  # us
 
 
+def op_cases(warmup: int = 10, iters: int = 30) -> dict:
+    """The reference's op metric on its own ten op cases: host wall-clock per call of
+    flash_attn_varlen_with_block_cu_bf16 (out allocated by the call, as there), timed with
+    perf_counter around the call and a synchronize (bench_attention_op.py:198-210), 10
+    warm-up and 30 timed calls; mean and median in ms. The reference's published numbers
+    for these cases are RTX 2050 timings of its v8 op (context only)."""
+    from toy_flash_attn import flash_attention_func as faf
+    from toy_flash_attn.workloads import REFERENCE_OP_CASES, reference_op_case
+
+    res = {}
+    for name in REFERENCE_OP_CASES:
+        c = reference_op_case(name).to("cuda")
+
+        def run():
+            return faf.flash_attn_varlen_with_block_cu_bf16(
+                q=c.q, k=c.k_cache, v=c.v_cache, max_seqlen_q=c.max_seqlen_q, cu_seqlens_q=c.cu_seqlens_q,
+                max_seqlen_k=c.max_seqlen_k, seqused_k=c.seqused_k, causal=c.causal, window_size=c.window_size,
+                block_table=c.block_table)
+
+        for _ in range(warmup):
+            run()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(iters):
+            t0 = time.perf_counter()
+            run()
+            torch.cuda.synchronize()
+            ts.append((time.perf_counter() - t0) * 1e3)
+        res[name] = {"ms_mean": round(statistics.mean(ts), 4), "ms_median": round(statistics.median(ts), 4)}
+    return res
+
+
 def side_configs(pk: dict) -> dict:
     from toy_flash_attn.workloads import baseline_config, kv_bytes, prefill_flops
 
@@ -709,6 +741,9 @@ def run_ours(args):
             del case
             torch.cuda.empty_cache()
             line["configs"] = side_configs(pk)
+            line["op_cases"] = {"metric": "host wall-clock ms per call (perf_counter + synchronize), the "
+                                          "reference's op benchmark method and cases",
+                                "cases": op_cases()}
             case = c5_shard(world, rank, args)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(case, args.cpu_seconds)

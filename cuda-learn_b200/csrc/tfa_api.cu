@@ -7,6 +7,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <cstddef>
 
 #include "../../include/tfa.h"
 #include "tfa_common.cuh"
@@ -313,6 +314,33 @@ int check_device(int dev) {
   return major == 10 ? TFA_OK : TFA_ERR_DEVICE;
 }
 
+
+// Per-host-thread cache of the last few calls' plans and tensor maps, keyed by the bytes of
+// the argument struct (every field up to num_splits: pointers, strides, sizes, flags) and
+// the device. A serving loop repeats the same call shape with the same cache and query
+// buffers, so a hit skips validation, planning and the tensor-map encodes (the maps embed
+// the K/V and q addresses, which are part of the key).
+constexpr size_t kKeyBytes = offsetof(tfa_fwd_params, num_splits) + sizeof(int32_t);
+struct CachedCall {
+  unsigned char key[kKeyBytes];
+  int dev;
+  bool valid;
+  FullPlan fp;
+  KvMaps maps;
+  CUtensorMap q_map;
+};
+constexpr int kCachedCalls = 8;
+thread_local CachedCall t_calls[kCachedCalls];
+thread_local unsigned t_next_call = 0;
+
+const CachedCall* find_call(const tfa_fwd_params* a, int dev) {
+  for (int i = 0; i < kCachedCalls; ++i) {
+    const CachedCall& c = t_calls[i];
+    if (c.valid && c.dev == dev && std::memcmp(c.key, a, kKeyBytes) == 0) return &c;
+  }
+  return nullptr;
+}
+
 }  // namespace
 }  // namespace tfa
 
@@ -364,6 +392,9 @@ int tfa_plan(const tfa_fwd_params* p, int device, tfa_plan_info* info) {
 }
 
 size_t tfa_workspace_size(const tfa_fwd_params* p, int device) {
+  if (p && device >= 0) {
+    if (const CachedCall* hit = find_call(p, device)) return hit->fp.ws_bytes;
+  }
   if (validate(p) != TFA_OK) return 0;
   FullPlan fp;
   if (make_plan(p, device, &fp) != TFA_OK) return 0;
@@ -373,6 +404,7 @@ size_t tfa_workspace_size(const tfa_fwd_params* p, int device) {
 }  // extern "C"
 
 namespace tfa {
+
 int workspace_zero_ranges(const tfa_fwd_params* p, int device, size_t off[2], size_t bytes[2]) {
   int rc = validate(p);
   if (rc != TFA_OK) return rc;
@@ -388,14 +420,36 @@ int workspace_zero_ranges(const tfa_fwd_params* p, int device, size_t off[2], si
 // Shared by every forward entry point: checks, plan, descriptors, launches.
 int fwd_impl(const tfa_fwd_params* a, void* workspace, size_t workspace_bytes, void* stream, void* ev_begin,
              void* ev_end) {
-  int rc = validate(a);
-  if (rc != TFA_OK) return rc;
-  if (a->batch == 0 || a->total_q == 0) return TFA_OK;
+  if (!a) return TFA_ERR_NULL_POINTER;
+  int rc = TFA_OK;
   int dev = 0;
-  if ((rc = current_device(&dev)) != TFA_OK) return rc;
-  if ((rc = check_device(dev)) != TFA_OK) return rc;
-  FullPlan fp;
-  if ((rc = make_plan(a, dev, &fp)) != TFA_OK) return rc;
+  const bool have_dev = current_device(&dev) == TFA_OK;
+  const CachedCall* hit = have_dev ? find_call(a, dev) : nullptr;
+  if (!hit) {
+    if ((rc = validate(a)) != TFA_OK) return rc;  // argument errors first, as before any CUDA call
+    if (a->batch == 0 || a->total_q == 0) return TFA_OK;
+    if (!have_dev) return TFA_ERR_CUDA;
+    if ((rc = check_device(dev)) != TFA_OK) return rc;
+    CachedCall& c = t_calls[t_next_call++ % kCachedCalls];
+    c.valid = false;
+    if ((rc = make_plan(a, dev, &c.fp)) != TFA_OK) return rc;
+    const int box_rows = a->block_size < 16 ? (int)a->block_size : 16;
+    if ((rc = encode_maps(a, box_rows, &c.maps)) != TFA_OK) return rc;
+    std::memset(&c.q_map, 0, sizeof(c.q_map));
+    const int64_t group = a->num_q_heads / a->num_kv_heads;
+    // decode kernel only: (64 columns, group heads, 16 / group tokens) boxes of q
+    if ((c.fp.pre.kernel == 0 || c.fp.mixed) && group <= 16 &&
+        encode_q_map(&c.q_map, a->q, a->total_q, a->num_q_heads, a->head_dim, a->q_stride[0], a->q_stride[1],
+                     (uint32_t)group, (uint32_t)(16 / group)) != 0)
+      return TFA_ERR_TENSOR_MAP;
+    std::memcpy(c.key, a, kKeyBytes);
+    c.dev = dev;
+    c.valid = true;
+    hit = &c;
+  }
+  const FullPlan& fp = hit->fp;
+  const KvMaps& maps = hit->maps;
+  const CUtensorMap& q_map = hit->q_map;
   if (!workspace || workspace_bytes < fp.ws_bytes || !aligned16(workspace)) return TFA_ERR_WORKSPACE;
   const Plan& pl = fp.pre;
   FwdParams p;
@@ -417,15 +471,6 @@ int fwd_impl(const tfa_fwd_params* a, void* workspace, size_t workspace_bytes, v
     p.seq_filter = 2;
     pd.seq_filter = 1;
   }
-  KvMaps maps;
-  if ((rc = encode_maps(a, p.box_rows, &maps)) != TFA_OK) return rc;
-  const bool any_decode = pl.kernel == 0 || fp.mixed;
-  CUtensorMap q_map;  // decode kernel only: (64 columns, group heads, 16 / group tokens) boxes of q
-  std::memset(&q_map, 0, sizeof(q_map));
-  if (any_decode &&
-      encode_q_map(&q_map, a->q, a->total_q, a->num_q_heads, a->head_dim, a->q_stride[0], a->q_stride[1],
-                   (uint32_t)p.group, (uint32_t)(16 / p.group)) != 0)
-    return TFA_ERR_TENSOR_MAP;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   cudaError_t e = cudaSuccess;
   auto fail = [&](cudaError_t err) {

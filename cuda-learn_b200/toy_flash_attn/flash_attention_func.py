@@ -19,6 +19,8 @@ from __future__ import annotations
 
 import ctypes
 import os
+import struct
+import threading
 from itertools import count
 from pathlib import Path
 
@@ -28,6 +30,7 @@ from . import _lib
 
 _CUDA_VALUE_DTYPE = torch.bfloat16
 _CUDA_INDEX_DTYPE = torch.int32
+_TFA_ERR_WORKSPACE = -7
 _DUMP_COUNTER = count()
 
 __all__ = [
@@ -185,10 +188,42 @@ def _workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor:
     return ws
 
 
+# struct tfa_fwd_params packed in one call (the fields in declaration order, native 64-bit
+# layout; the trailing 4 bytes are the struct's padding)
+_PARAM_FMT = "=Q3qQ4qQ4qQ3qQQQQ10q3ifi4x"
+assert struct.calcsize(_PARAM_FMT) == ctypes.sizeof(_lib.TfaFwdParams)
+_tls = threading.local()
+
+
+def _current_raw_stream(device_index: int) -> int:
+    """The current CUDA stream of a device as an integer handle."""
+    raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    if raw is not None:
+        return raw(device_index)
+    return torch.cuda.current_stream(device_index).cuda_stream
+
+
 def _fill_params(
     q, k, v, out, cu_seqlens_q, seqused_k, block_table, max_seqlen_q, max_seqlen_k, causal, window_size,
-    softmax_lse, softmax_scale, num_splits,
+    softmax_lse, softmax_scale, num_splits, reuse: bool = False,
 ) -> _lib.TfaFwdParams:
+    """Argument struct of one call. With ``reuse`` the struct object is this thread's
+    scratch copy, overwritten by its next call (the hot path packs it in one step)."""
+    if reuse:
+        p = getattr(_tls, "params", None)
+        if p is None:
+            p = _tls.params = _lib.TfaFwdParams()
+        wl, wr = (-1, -1) if window_size is None else (int(window_size[0]), int(window_size[1]))
+        qs, ks, vs, os_ = q.stride(), k.stride(), v.stride(), out.stride()
+        struct.pack_into(
+            _PARAM_FMT, p, 0,
+            q.data_ptr(), *qs, k.data_ptr(), *ks, v.data_ptr(), *vs, out.data_ptr(), *os_,
+            softmax_lse.data_ptr() if softmax_lse is not None else 0,
+            cu_seqlens_q.data_ptr(), seqused_k.data_ptr(), block_table.data_ptr(), block_table.stride(0),
+            seqused_k.numel(), q.shape[0], q.shape[1], k.shape[2], q.shape[2], k.shape[1], k.shape[0],
+            int(max_seqlen_q), int(max_seqlen_k), 1 if causal else 0, wl, wr,
+            float(softmax_scale) if softmax_scale is not None else 0.0, int(num_splits))
+        return p
     p = _lib.TfaFwdParams()
     p.q = q.data_ptr()
     p.q_stride[:] = list(q.stride())
@@ -267,13 +302,12 @@ def flash_attn_varlen_with_block_cu_bf16(
     _maybe_log_cuda_inputs(q=q, k=k, v=v, cu_seqlens_q=cu_seqlens_q, seqused_k=seqused_k,
                            block_table=block_table, out=out)
     dev = q.device
-    _check_cuda_tensor("q", q, expected_device=dev, expected_dtype=_CUDA_VALUE_DTYPE)
-    _check_cuda_tensor("k", k, expected_device=dev, expected_dtype=_CUDA_VALUE_DTYPE)
-    _check_cuda_tensor("v", v, expected_device=dev, expected_dtype=_CUDA_VALUE_DTYPE)
-    _check_cuda_tensor("cu_seqlens_q", cu_seqlens_q, expected_device=dev, expected_dtype=_CUDA_INDEX_DTYPE)
-    _check_cuda_tensor("seqused_k", seqused_k, expected_device=dev, expected_dtype=_CUDA_INDEX_DTYPE)
-    _check_cuda_tensor("block_table", block_table, expected_device=dev, expected_dtype=_CUDA_INDEX_DTYPE)
-    _check_cuda_tensor("out", out, expected_device=dev, expected_dtype=_CUDA_VALUE_DTYPE)
+    di = q.get_device()
+    for name, t, dt in (("q", q, _CUDA_VALUE_DTYPE), ("k", k, _CUDA_VALUE_DTYPE), ("v", v, _CUDA_VALUE_DTYPE),
+                        ("cu_seqlens_q", cu_seqlens_q, _CUDA_INDEX_DTYPE), ("seqused_k", seqused_k, _CUDA_INDEX_DTYPE),
+                        ("block_table", block_table, _CUDA_INDEX_DTYPE), ("out", out, _CUDA_VALUE_DTYPE)):
+        if t.get_device() != di or t.dtype is not dt:
+            _check_cuda_tensor(name, t, expected_device=dev, expected_dtype=dt)  # raises with the reference's message
     _check_gqa_heads(q, k, v, out)
     if q.shape != out.shape:
         raise ValueError(f"q and out must have the same shape, got {tuple(q.shape)} and {tuple(out.shape)}")
@@ -292,23 +326,30 @@ def flash_attn_varlen_with_block_cu_bf16(
 
     lib = _lib.load()
     p = _fill_params(q, k, v, out, cu_seqlens_q, seqused_k, block_table, max_seqlen_q, max_seqlen_k, causal,
-                     window_size, softmax_lse, softmax_scale, num_splits)
-    with torch.cuda.device(dev):
-        stream = torch.cuda.current_stream(dev).cuda_stream
-        need = lib.tfa_workspace_size(ctypes.byref(p), dev.index)
-        if need == 0 and q.shape[0] > 0 and seqused_k.numel() > 0:
-            # invalid arguments: let tfa_fwd report the precise status
-            need = 4096
-        ws = _workspace(dev, stream, need)
+                     window_size, softmax_lse, softmax_scale, num_splits, reuse=True)
+    prev = torch.cuda.current_device()
+    if prev != di:
+        torch.cuda.set_device(di)
+    try:
+        stream = _current_raw_stream(di)
+        ws = _workspace(dev, stream, 0)
         if main_events is None:
-            _lib.check(lib.tfa_fwd(ctypes.byref(p), ws.data_ptr(), ws.numel(), stream), "tfa_fwd")
+            rc = lib.tfa_fwd(ctypes.byref(p), ws.data_ptr(), ws.numel(), stream)
+            if rc == _TFA_ERR_WORKSPACE:  # first call of a larger shape on this stream: grow and retry
+                ws = _workspace(dev, stream, max(lib.tfa_workspace_size(ctypes.byref(p), di), 4096))
+                rc = lib.tfa_fwd(ctypes.byref(p), ws.data_ptr(), ws.numel(), stream)
+            _lib.check(rc, "tfa_fwd")
         else:
+            ws = _workspace(dev, stream, max(lib.tfa_workspace_size(ctypes.byref(p), di), 4096))
             ev0, ev1 = main_events
             for ev in (ev0, ev1):
                 if not ev.cuda_event:  # torch creates the event on its first record
                     ev.record()
             _lib.check(lib.tfa_fwd_timed(ctypes.byref(p), ws.data_ptr(), ws.numel(), stream, ev0.cuda_event,
                                          ev1.cuda_event), "tfa_fwd_timed")
+    finally:
+        if prev != di:
+            torch.cuda.set_device(prev)
     _maybe_dump_flash_attn_context(
         "with_block_cu",
         q=q, k=k, v=v, max_seqlen_q=max_seqlen_q, cu_seqlens_q=cu_seqlens_q, max_seqlen_k=max_seqlen_k,

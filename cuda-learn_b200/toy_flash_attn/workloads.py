@@ -23,7 +23,7 @@ from dataclasses import dataclass, replace
 import torch
 
 __all__ = ["PagedCase", "reference_case", "baseline_config", "c5_kv_lengths", "BASELINE_CONFIGS", "kv_bytes",
-           "prefill_flops", "compact_sample", "verify_sequences"]
+           "prefill_flops", "compact_sample", "verify_sequences", "REFERENCE_OP_CASES", "reference_op_case"]
 
 
 @dataclass
@@ -329,3 +329,26 @@ def verify_sequences(kv_lens: list[int], n_longest: int = 16, n_random: int = 16
     g = torch.Generator().manual_seed(seed)
     pick = torch.randperm(len(rest), generator=g)[:n_random].tolist()
     return sorted(longest + [rest[i] for i in pick])
+
+
+# The reference's op-benchmark cases (flash_attention_backend/bench/op/cases_op.py:20-141):
+# name -> (q_lens, k_lens, num_heads, num_kv_heads, head_dim, causal, window_size, seed); its
+# bench builds them with make_block_cache at block_size 16 (bench_attention_op.py:120-125).
+REFERENCE_OP_CASES = {
+    "qwen_like_b1_s128_h64": ([1], [128], 14, 2, 64, True, None, 0),
+    "qwen_like_b4_s128_h64": ([1] * 4, [128] * 4, 14, 2, 64, True, None, 0),
+    "qwen_like_b1_s512_h64": ([1], [512], 14, 2, 64, True, None, 0),
+    "qwen_like_b4_s512_h64": ([1] * 4, [512] * 4, 14, 2, 64, True, None, 0),
+    "qwen_like_b1_s2048_h64": ([1], [2048], 14, 2, 64, True, None, 1),
+    "mha_b1_s2048_h64_h14_kv14": ([1], [2048], 14, 14, 64, True, None, 1),
+    "single_head_b1_s2048_h64_h1_kv1": ([1], [2048], 1, 1, 64, True, None, 1),
+    "gpt2_like_b1_s128_h64": ([1], [128], 12, 12, 64, True, None, 0),
+    "gqa_case_b1_s128": ([1], [128], 8, 2, 64, True, (64, 0), 7),
+    "gqa_case_b4_s512": ([1] * 4, [512, 384, 512, 256], 8, 2, 64, True, None, 9),
+}
+
+
+def reference_op_case(name: str) -> PagedCase:
+    q_lens, k_lens, hq, hkv, d, causal, window, seed = REFERENCE_OP_CASES[name]
+    return reference_case(q_lens, k_lens, num_heads=hq, num_kv_heads=hkv, head_dim=d, causal=causal,
+                          window_size=window, block_size=16, seed=seed, name=name)
