@@ -98,6 +98,7 @@ __global__ void __launch_bounds__(1024) item_list_kernel(const __grid_constant__
   constexpr int kKeys = 65;
   __shared__ int hist[kKeys];
   __shared__ int base[kKeys];
+  if (threadIdx.x == 0) allow_dependent_launch();  // the decode kernel's set-up overlaps this kernel
   const int groups = p.q_tiles * p.batch * p.hkv;
   for (int i = threadIdx.x; i < kKeys; i += blockDim.x) hist[i] = 0;
   __syncthreads();

@@ -156,6 +156,14 @@ __device__ __forceinline__ void scheduler_finish(const FwdParams& p) {
   }
 }
 
+// Programmatic dependent launch: lets the next kernel on the stream (the split-KV combine
+// after an attention kernel, the decode kernel after the item-list kernel) be scheduled
+// before this grid finishes; the dependent waits with grid_dependency_wait().
+__device__ __forceinline__ void allow_dependent_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // ---------------------------------------------------------------------------
 // Paged K/V gather: a producer warp fetches the 128-token tile of kv head h of sequence b
 // page group by page group (one TMA box per 16-slot group and 64 columns). One tile of one
@@ -320,7 +328,12 @@ __device__ __forceinline__ void producer_loop(const FwdParams& p, const KvMaps& 
   int c = 0;
   // item indices handed out: the device-built list's length, or every slot
   int bound = p.num_items;
-  if constexpr (kList) bound = *reinterpret_cast<const volatile int*>(p.item_count);
+  if constexpr (kList) {
+    // This instance is launched as a programmatic dependent of the list kernel: its set-up
+    // overlapped that kernel; the list and its length are read only after it completed.
+    grid_dependency_wait();
+    bound = *reinterpret_cast<const volatile int*>(p.item_count);
+  }
   int claimed = (lane == 0) ? (int)blockIdx.x : 0;  // next item index (lane 0)
   auto claim = [&]() {
     if (lane == 0) claimed = atomicAdd(&p.sched[0], 1) + (int)gridDim.x;
@@ -528,12 +541,6 @@ __device__ __forceinline__ void producer_follow_kv_slots(const FwdParams& p, con
   }
 }
 
-// Programmatic dependent launch: lets the next kernel on the stream (the split-KV combine)
-// be scheduled before this grid finishes; the dependent waits with grid_dependency_wait().
-__device__ __forceinline__ void allow_dependent_launch() {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
-__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll

@@ -38,6 +38,8 @@ constexpr int kNP = 16;  // packed q rows (MMA N)
 __device__ unsigned long long g_decode_stamp[32];
 __device__ unsigned long long g_decode_tile[16][12];
 __device__ unsigned long long g_decode_end[512];
+__device__ unsigned long long g_decode_begin[512];
+__device__ int g_decode_ntiles[512];
 #define STAMP(i) do { if (blockIdx.x == 0) g_decode_stamp[i] = global_timer_ns(); } while (0)
 #define PH(cj, i) do { if (blockIdx.x == 0 && (cj) < 16) g_decode_tile[cj][i] = global_timer_ns(); } while (0)
 }  // namespace
@@ -170,6 +172,9 @@ __global__ void __launch_bounds__(224, 1)
   const int warp = tid >> 5;
   const int lane = tid & 31;
   if (tid == 0) STAMP(0);
+#ifdef TFA_PROFILE
+  const unsigned long long t_begin_prof = global_timer_ns();
+#endif
   if constexpr (kMode != 1) {
     // The first item of this CTA is item blockIdx.x: bring its sequence's lengths and the
     // start of its block-table row into L2 while the CTA sets up (the producer's first
@@ -560,6 +565,9 @@ __global__ void __launch_bounds__(224, 1)
       if (lane == 0) mbar_arrive(&item_empty[slot]);
     }
     if (warp == 2 && lane == 0) STAMP(12);
+#ifdef TFA_PROFILE
+    if (warp == 2 && lane == 0 && blockIdx.x < 512) g_decode_ntiles[blockIdx.x] = c;
+#endif
   }
 
   if (abort_flag && (warp == 0 || warp == 6)) {
@@ -578,6 +586,7 @@ __global__ void __launch_bounds__(224, 1)
   if (tid == 0) STAMP(14);
 #ifdef TFA_PROFILE
   if (tid == 0 && blockIdx.x < 512) g_decode_end[blockIdx.x] = global_timer_ns();
+  if (tid == 0 && blockIdx.x < 512) g_decode_begin[blockIdx.x] = t_begin_prof;
 #endif
 }
 
@@ -605,6 +614,21 @@ cudaError_t launch_decode(const FwdParams& p, const KvMaps& maps, const CUtensor
       configured[dev][mode] = true;
     }
   }
+  if (mode == 1) {
+    // after the item-list kernel, as its programmatic dependent (the list is read only after
+    // griddepcontrol.wait in the producer)
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(224);
+    cfg.dynamicSmemBytes = DecodeCfg<D>::kDynBytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, p, maps, q_map);
+  }
   kernel<<<grid, 224, DecodeCfg<D>::kDynBytes, s>>>(p, maps, q_map);
   return cudaGetLastError();
 }
@@ -615,6 +639,11 @@ extern "C" __attribute__((visibility("default"))) int tfa_decode_stamps_read(uns
 }
 extern "C" __attribute__((visibility("default"))) int tfa_decode_tiles_read(unsigned long long* host) {
   return (int)cudaMemcpyFromSymbol(host, g_decode_tile, sizeof(g_decode_tile));
+}
+extern "C" __attribute__((visibility("default"))) int tfa_decode_cta_read(unsigned long long* b, unsigned long long* e, int* n) {
+  cudaMemcpyFromSymbol(b, g_decode_begin, sizeof(g_decode_begin));
+  cudaMemcpyFromSymbol(n, g_decode_ntiles, sizeof(g_decode_ntiles));
+  return (int)cudaMemcpyFromSymbol(e, g_decode_end, sizeof(g_decode_end));
 }
 extern "C" __attribute__((visibility("default"))) int tfa_decode_ends_read(unsigned long long* host) {
   cudaError_t e = cudaMemcpyFromSymbol(host, g_decode_end, sizeof(g_decode_end));
