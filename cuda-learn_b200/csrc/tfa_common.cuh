@@ -388,6 +388,9 @@ __device__ __forceinline__ void producer_loop(const FwdParams& p, const KvMaps& 
         if (lane == 0) mbar_arrive_expect_tx(&full[st], KvStage<D>::kTensorBytes);
         __syncwarp();
         if (lane < groups) issue_group_one<D>(p, maps, w, lane, cur, 1, ring + st * KvStage<D>::kTensorBytes, &full[st], policy);
+#ifdef TFA_PROFILE
+        if (lane == 0 && p.rows_per_tile == 16) decode_tile_hook(c, 0);
+#endif
         cur = nxt;
       }
     } else {
