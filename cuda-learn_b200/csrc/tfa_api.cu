@@ -266,6 +266,7 @@ void fill_params(const tfa_fwd_params* a, const Plan& pl, void* ws, FwdParams* p
   p->hkv = (int)a->num_kv_heads;
   p->group = (int)(a->num_q_heads / a->num_kv_heads);
   p->block_size = (int)a->block_size;
+  p->max_seqlen_k_pages = (int)((a->max_seqlen_k + a->block_size - 1) / a->block_size);
   p->box_rows = a->block_size < 16 ? (int)a->block_size : 16;
   p->num_blocks = (int)a->num_blocks;
   p->causal = a->causal ? 1 : 0;

@@ -53,6 +53,7 @@ struct FwdParams {
   const int* item_list;    // decode kernel: existing items (g * max_splits + split), longest
                            // first, built on the device for the call (NULL: slot order)
   const int* item_count;   // number of entries of item_list
+  int max_seqlen_k_pages;   // block-table entries a sequence may use (prefetch bound)
   int* group_cnt;          // decode kernel instance that merges in-kernel: per work group, splits
                            // finished so far (self-resetting); the last one merges the group
 };

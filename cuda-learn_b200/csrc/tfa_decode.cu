@@ -185,6 +185,15 @@ __global__ void __launch_bounds__(224, 1)
                     : lane == 1 ? (const void*)(p.seqused_k + b) : (const void*)(p.block_table + (int64_t)b * p.bt_s0);
       prefetch_l2(a);
     }
+    // warp 6 (the V producer, idle until the first item is published) brings the rest of
+    // that sequence's block-table row into L2: a split's or a window's first page lies
+    // anywhere in it
+    if (warp == 6) {
+      const int b = (int)((blockIdx.x / (unsigned)p.hkv) % (unsigned)p.batch);
+      const int64_t pages = p.max_seqlen_k_pages;
+      for (int64_t i = 32 * (1 + lane); i < pages && i < 32 * 64; i += 32 * 32)
+        prefetch_l2(p.block_table + (int64_t)b * p.bt_s0 + i);
+    }
   }
 
   if (tid == 0) {
