@@ -71,8 +71,11 @@ def _static_call(c, num_splits=0):
         (lambda: reference_case([1, 9], [700, 90], num_heads=8, num_kv_heads=2, head_dim=128, causal=True,
                                 block_size=16, seed=3), 0),
         (_item_list_case, 0),                                # decode kernel with the device-built item list
+        (lambda: reference_case([1, 1, 1, 40, 1, 1, 1, 2], [900, 700, 1200, 300, 129, 800, 60, 90], num_heads=8,
+                                num_kv_heads=2, head_dim=64, causal=True, block_size=16, seed=8), 0),
+                                                             # both kernels in one call (chunked prefill)
     ],
-    ids=["C2", "C3_split3", "C4_b8", "hd128_mixed", "item_list"],
+    ids=["C2", "C3_split3", "C4_b8", "hd128_mixed", "item_list", "mixed_dispatch"],
 )
 def test_static_workspace_matches_tfa_fwd_twice(make, splits):
     case = make()
