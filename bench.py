@@ -39,7 +39,7 @@ UNIT = "TB/s"
 L2_BYTES = 126 * 1024 * 1024
 # DRAM bytes (read + write) of one decode_kernel launch per algorithmic K/V byte, from an
 # ncu capture of the decode kernel on a reduced C5 (traffic grows with the K/V bytes read).
-TRAFFIC_PER_KV_BYTE = (471.89e6 + 6.53e6) / 471.49e6
+TRAFFIC_PER_KV_BYTE = (471.91e6 + 4.19e6) / 471.49e6
 
 
 def parse_args():
