@@ -102,6 +102,32 @@ def test_c5_reduced_batch_full_lengths():
     assert_parity(case)
 
 
+@pytest.mark.parametrize("hq, hkv, hd, bs, q_lens", [
+    (32, 8, 128, 16, [1, 1]),       # C5 heads: 16384 pages in one block-table row
+    (14, 2, 64, 256, [1, 2]),       # the reference's heads, large pages, a 2-token chunk (14 rows)
+])
+def test_long_context_decode(hq, hkv, hd, bs, q_lens):
+    """Decode against a 262144-token context (and a 100003-token one): tile, position and
+    block-table index arithmetic well past the BASELINE lengths, splits at their cap."""
+    case = reference_case(q_lens, [262144, 100003], num_heads=hq, num_kv_heads=hkv, head_dim=hd, causal=True,
+                          block_size=bs, seed=21, name="long_context")
+    p = faf.plan(case.q.cuda(), case.k_cache.cuda(), case.v_cache.cuda(), case.cu_seqlens_q.cuda(),
+                 case.seqused_k.cuda(), case.block_table.cuda(), case.max_seqlen_q, case.max_seqlen_k, True)
+    assert p["kernel"] == 0 and p["max_splits"] > 1
+    assert_parity(case)
+
+
+@pytest.mark.parametrize("q_len", [1, 3])
+def test_wide_batch_decode(q_len):
+    """4096 short sequences in one call (16384 work groups): the persistent scheduler, the
+    split bookkeeping and the combine over far more groups than the in-kernel merge counts."""
+    g = torch.Generator().manual_seed(33)
+    k_lens = torch.randint(1, 300, (4096,), generator=g).tolist()
+    case = reference_case([q_len] * 4096, [max(k, q_len) for k in k_lens], num_heads=16, num_kv_heads=4,
+                          causal=True, block_size=16, seed=33, name="wide_batch")
+    assert_parity(case)
+
+
 def test_c5_full_size_sample_vs_oracle():
     """The headline call at full size: all 256 sequences, the 2^21-block pool (137 GB of
     K/V), one call. The 16 longest and 16 seeded-random sequences are checked against the
