@@ -81,11 +81,6 @@ __device__ __forceinline__ void warpgroup_reg_claim() {
   asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
 }
 
-// Named barrier over a subset of the CTA's warps (id 0 is __syncthreads).
-__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
-}
-
 // Makes generic-proxy shared-memory writes visible to the async proxy (TMA / tcgen05).
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -312,11 +307,6 @@ __device__ __forceinline__ void tmem_ld128_sync(uint32_t taddr, float (&v)[128])
       : "memory");
 #pragma unroll
   for (int i = 0; i < 128; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-// TMEM address of (lane, column) relative to an allocation base.
-__device__ __forceinline__ uint32_t tmem_addr(uint32_t base, uint32_t lane, uint32_t col) {
-  return base + (lane << 16) + col;
 }
 
 // ---------------------------------------------------------------------------
