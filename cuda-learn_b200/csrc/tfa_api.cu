@@ -25,6 +25,9 @@ constexpr size_t kCtrlBytes = 256;  // workspace control block: sched[2], err, d
 constexpr size_t kCounterRegionEnd = 64 * 1024;
 constexpr int64_t kMaxCountedGroups = (int64_t)((kCounterRegionEnd - kCtrlBytes) / sizeof(int));
 constexpr int kMaxDevices = 128;
+#ifndef TFA_PAGE_DECODE
+#define TFA_PAGE_DECODE 1
+#endif
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
@@ -79,6 +82,7 @@ struct Plan {
   int rows, q_tiles, max_splits, split_cap, num_items, grid;
   int combine;         // 0: no splits; 1: the combine kernel merges them; 2: the decode kernel does
   int item_list;       // decode with splits and many slots: a device-built, longest-first item list
+  int pages;           // decode over whole pages (all kv heads per item): decode_page_kernel
   size_t cnt_off;      // byte offset of the per-group split counters (combine == 2)
   size_t lse_off, o_off;  // byte offsets of the split partials
   size_t list_off;     // byte offset of the item list
@@ -146,10 +150,28 @@ int make_plan_one(const tfa_fwd_params* p, int device, Plan* pl) {
       }
     }
   }
+  // Large decode calls over whole pages (8 kv heads x 16 slots = one 128-row tile per page,
+  // one q token per sequence): an item carries all kv heads of a sequence's split, so
+  // splits are counted per sequence and the per-head kernel's cap is divided by the kv
+  // heads (about the same bytes per item). It reads each page as one contiguous box and
+  // issues a quarter of the exponentials per byte; on C5 (one B200) it matches the per-head
+  // kernel in a short burst and streams 1.8 % faster over a second of calls under the
+  // power cap. Latency-bound calls stay on the per-head kernel, which needs no split
+  // (C4: 24 vs 34 us per call on the page kernel with splits and the combine).
+  pl->pages = (TFA_PAGE_DECODE && decode && p->max_seqlen_q == 1 && p->num_splits == 0 &&
+               est_all >= 32 * (int64_t)sms &&
+               page_decode_supported((int)p->head_dim, (int)p->num_kv_heads, (int)p->block_size, (int)G))
+                  ? 1
+                  : 0;
+  if (pl->pages) {
+    cap /= p->num_kv_heads;
+    if (cap < 1) cap = 1;
+    S = (tiles + cap - 1) / cap;
+  }
   if (S < 1) S = 1;
   pl->max_splits = (int)S;
   pl->split_cap = (int)cap;
-  const int64_t items = S * pl->q_tiles * p->batch * p->num_kv_heads;
+  const int64_t items = S * pl->q_tiles * p->batch * (pl->pages ? 1 : p->num_kv_heads);
   if (items > INT32_MAX / 2) return TFA_ERR_SHAPE;
   pl->num_items = (int)items;
   pl->grid = (int)(items < sms ? items : sms);
@@ -162,7 +184,7 @@ int make_plan_one(const tfa_fwd_params* p, int device, Plan* pl) {
   // count and merge inside the kernel cost more (C5 on one B200: +3.7 % per call).
   const int64_t groups = (int64_t)p->batch * p->num_kv_heads * pl->q_tiles;
   const bool latency_bound = est_all < 32 * (int64_t)sms;
-  pl->combine = S > 1 ? ((decode && latency_bound && groups <= kMaxCountedGroups) ? 2 : 1) : 0;
+  pl->combine = S > 1 ? ((decode && !pl->pages && latency_bound && groups <= kMaxCountedGroups) ? 2 : 1) : 0;
   size_t ws = kCtrlBytes;
   pl->cnt_off = pl->lse_off = pl->o_off = 0;
   if (S > 1) {
@@ -184,7 +206,7 @@ int make_plan_one(const tfa_fwd_params* p, int device, Plan* pl) {
   // (a C5 shard at 4 or 8 GPUs: -4.6 % per call); on larger calls the extra launch costs
   // more than the tail it saves.
   pl->item_list =
-      (decode && pl->combine == 1 && items > 2 * (int64_t)sms && est_all < 1024 * (int64_t)sms) ? 1 : 0;
+      (decode && !pl->pages && pl->combine == 1 && items > 2 * (int64_t)sms && est_all < 1024 * (int64_t)sms) ? 1 : 0;
   pl->list_off = 0;
   if (pl->item_list) {
     pl->list_off = align_up(ws, 256);
@@ -228,6 +250,7 @@ int make_plan(const tfa_fwd_params* p, int device, FullPlan* fp) {
     d.max_seqlen_q = 16 / G;  // the decode kernel's sequences are at most this long
     if ((rc = make_plan_one(&d, device, &fp->dec)) != TFA_OK) return rc;
     fp->dec.item_list = 0;  // the decode part of a mixed call keeps slot order
+    fp->dec.pages = 0;
     if (fp->dec.ws_bytes > fp->dec.list_off && fp->dec.list_off) fp->dec.ws_bytes = fp->dec.list_off;
     // the decode part counts its groups in the call's own counter region, so the call
     // reserves it whenever the decode part has splits
@@ -293,13 +316,18 @@ void fill_params(const tfa_fwd_params* a, const Plan& pl, void* ws, FwdParams* p
   if (pl.combine == 2) p->group_cnt = reinterpret_cast<int*>(w + pl.cnt_off);
 }
 
-int encode_maps(const tfa_fwd_params* a, int box_rows, KvMaps* m) {
+int encode_maps(const tfa_fwd_params* a, int box_rows, bool pages, KvMaps* m) {
   const int64_t ks[3] = {a->k_stride[0], a->k_stride[1], a->k_stride[2]};
   const int64_t vs[3] = {a->v_stride[0], a->v_stride[1], a->v_stride[2]};
   if (encode_kv_map(&m->k_box, a->k, a->num_blocks, a->block_size, a->num_kv_heads, a->head_dim, ks, box_rows) ||
       encode_kv_map(&m->k_row, a->k, a->num_blocks, a->block_size, a->num_kv_heads, a->head_dim, ks, 1) ||
       encode_kv_map(&m->v_box, a->v, a->num_blocks, a->block_size, a->num_kv_heads, a->head_dim, vs, box_rows) ||
       encode_kv_map(&m->v_row, a->v, a->num_blocks, a->block_size, a->num_kv_heads, a->head_dim, vs, 1))
+    return TFA_ERR_TENSOR_MAP;
+  std::memset(&m->k_page, 0, sizeof(m->k_page));
+  std::memset(&m->v_page, 0, sizeof(m->v_page));
+  if (pages && (encode_page_map(&m->k_page, a->k, a->num_blocks, a->block_size, a->num_kv_heads, a->head_dim, ks) ||
+                encode_page_map(&m->v_page, a->v, a->num_blocks, a->block_size, a->num_kv_heads, a->head_dim, vs)))
     return TFA_ERR_TENSOR_MAP;
   return TFA_OK;
 }
@@ -389,6 +417,7 @@ int tfa_plan(const tfa_fwd_params* p, int device, tfa_plan_info* info) {
   info->combine = pl.combine;
   info->workspace_bytes = fp.ws_bytes;
   info->item_list = pl.item_list;
+  info->pages = pl.pages;
   return TFA_OK;
 }
 
@@ -435,14 +464,20 @@ int fwd_impl(const tfa_fwd_params* a, void* workspace, size_t workspace_bytes, v
     c.valid = false;
     if ((rc = make_plan(a, dev, &c.fp)) != TFA_OK) return rc;
     const int box_rows = a->block_size < 16 ? (int)a->block_size : 16;
-    if ((rc = encode_maps(a, box_rows, &c.maps)) != TFA_OK) return rc;
+    if ((rc = encode_maps(a, box_rows, c.fp.pre.pages != 0, &c.maps)) != TFA_OK) return rc;
     std::memset(&c.q_map, 0, sizeof(c.q_map));
     const int64_t group = a->num_q_heads / a->num_kv_heads;
-    // decode kernel only: (64 columns, group heads, 16 / group tokens) boxes of q
-    if ((c.fp.pre.kernel == 0 || c.fp.mixed) && group <= 16 &&
-        encode_q_map(&c.q_map, a->q, a->total_q, a->num_q_heads, a->head_dim, a->q_stride[0], a->q_stride[1],
-                     (uint32_t)group, (uint32_t)(16 / group)) != 0)
+    if (c.fp.pre.pages) {
+      // page decode kernel: one box of all the token's q heads (padded to the MMA's N)
+      if (encode_q_map(&c.q_map, a->q, a->total_q, a->num_q_heads, a->head_dim, a->q_stride[0], a->q_stride[1],
+                       (uint32_t)page_decode_cols((int)group), 1u) != 0)
+        return TFA_ERR_TENSOR_MAP;
+    } else if ((c.fp.pre.kernel == 0 || c.fp.mixed) && group <= 16 &&
+               encode_q_map(&c.q_map, a->q, a->total_q, a->num_q_heads, a->head_dim, a->q_stride[0], a->q_stride[1],
+                            (uint32_t)group, (uint32_t)(16 / group)) != 0) {
+      // decode kernel: (64 columns, group heads, 16 / group tokens) boxes of q
       return TFA_ERR_TENSOR_MAP;
+    }
     std::memcpy(c.key, a, kKeyBytes);
     c.dev = dev;
     c.valid = true;
@@ -490,7 +525,9 @@ int fwd_impl(const tfa_fwd_params* a, void* workspace, size_t workspace_bytes, v
     if (e != cudaSuccess) return fail(e);
   }
   const int mode = pl.item_list ? 1 : (pl.combine == 2 ? 2 : 0);  // decode kernel instance
-  if (a->head_dim == 64)
+  if (pl.pages)
+    e = launch_decode_pages((int)a->head_dim, (int)(a->num_q_heads / a->num_kv_heads), p, maps, q_map, pl.grid, s);
+  else if (a->head_dim == 64)
     e = pl.kernel == 0 ? launch_decode<64>(p, maps, q_map, pl.grid, s, mode) : launch_prefill<64>(p, maps, pl.grid, s);
   else
     e = pl.kernel == 0 ? launch_decode<128>(p, maps, q_map, pl.grid, s, mode) : launch_prefill<128>(p, maps, pl.grid, s);
@@ -563,7 +600,7 @@ int tfa_gather_kv(const tfa_fwd_params* a, const int64_t* kv_offsets, void* k_ou
   FwdParams p;
   fill_params(&b, pl, workspace, &p);
   KvMaps maps;
-  if ((rc = encode_maps(&b, p.box_rows, &maps)) != TFA_OK) return rc;
+  if ((rc = encode_maps(&b, p.box_rows, false, &maps)) != TFA_OK) return rc;
   const int max_tiles = (int)((b.max_seqlen_k + kBN - 1) / kBN);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   cudaError_t e = b.head_dim == 64 ? launch_gather<64>(p, maps, max_tiles, kv_offsets, k_out, v_out, s)

@@ -183,6 +183,9 @@ struct KvStage {
 
 struct KvMaps {
   CUtensorMap k_box, k_row, v_box, v_row;
+  // whole pages, rows head-major (dims head_dim, slot, kv head, block): the page decode
+  // kernel's boxes (encoded only for calls that use it)
+  CUtensorMap k_page, v_page;
 };
 
 // Page and row count of 16-slot group g (box_rows slots when block_size < 16) of a tile.
@@ -589,6 +592,12 @@ template <int D>
 cudaError_t launch_prefill(const FwdParams& p, const KvMaps& maps, int grid, cudaStream_t s);
 template <int D>
 cudaError_t launch_combine(const FwdParams& p, int max_rows, cudaStream_t s);
+// Page decode kernel (8 kv heads, 16-slot pages, one q token per sequence): whether a
+// shape is supported, its MMA N (q heads per token, padded), and the launch.
+bool page_decode_supported(int head_dim, int num_kv_heads, int block_size, int group);
+int page_decode_cols(int group);
+cudaError_t launch_decode_pages(int head_dim, int group, const FwdParams& p, const KvMaps& maps,
+                                const CUtensorMap& q_map, int grid, cudaStream_t s);
 cudaError_t launch_item_list(const FwdParams& p, int* list, int* count, cudaStream_t s);
 template <int D>
 cudaError_t launch_gather(const FwdParams& p, const KvMaps& maps, int max_tiles, const int64_t* kv_offsets,

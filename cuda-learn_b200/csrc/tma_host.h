@@ -55,6 +55,26 @@ inline int encode_kv_map(CUtensorMap* map, const void* base, int64_t num_blocks,
   return (int)r;
 }
 
+// Whole pages for the page decode kernel: the same cache, with the dimensions listed as
+// (head_dim, slot, kv_head, block) so that a box of (64 columns, all slots, all kv heads,
+// 1 block) lands head-major (row = kv_head * block_size + slot) as rows of 128 bytes with
+// the 128-byte swizzle. A full page is one box per 64-column panel.
+inline int encode_page_map(CUtensorMap* map, const void* base, int64_t num_blocks, int64_t block_size,
+                           int64_t num_kv_heads, int64_t head_dim, const int64_t strides_elems[3]) {
+  auto fn = get_encode_tiled();
+  if (!fn) return -1;
+  cuuint64_t dims[4] = {(cuuint64_t)head_dim, (cuuint64_t)block_size, (cuuint64_t)num_kv_heads,
+                        (cuuint64_t)num_blocks};
+  cuuint64_t strides[3] = {(cuuint64_t)strides_elems[1] * 2, (cuuint64_t)strides_elems[2] * 2,
+                           (cuuint64_t)strides_elems[0] * 2};
+  cuuint32_t box[4] = {64, (cuuint32_t)block_size, (cuuint32_t)num_kv_heads, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return (int)r;
+}
+
 // Query rows for the decode kernel: q is [total_q, num_q_heads, head_dim] bf16 with
 // element strides (token, head) and a contiguous head_dim. The map is 3-D, innermost
 // first (head_dim, q_head, token); a box is (64 columns, group heads, tokens) and lands

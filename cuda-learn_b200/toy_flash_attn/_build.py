@@ -19,7 +19,8 @@ LIB_NAME = "libtfa_sm100.so"
 LIB_PATH = PKG_DIR / LIB_NAME
 BUILD_DIR = PKG_DIR.parent / "_build"
 
-SOURCES = ["tfa_api.cu", "tfa_decode.cu", "tfa_prefill.cu", "tfa_aux.cu", "tfa_cache.cu", "tfa_noalloc.cu"]
+SOURCES = ["tfa_api.cu", "tfa_decode.cu", "tfa_decode_pages.cu", "tfa_prefill.cu", "tfa_aux.cu", "tfa_cache.cu",
+           "tfa_noalloc.cu"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-std=c++17", "-lineinfo",

@@ -97,6 +97,7 @@ class TfaPlanInfo(ctypes.Structure):
         ("combine", _i32),
         ("workspace_bytes", ctypes.c_uint64),
         ("item_list", _i32),
+        ("pages", _i32),
     ]
 
 

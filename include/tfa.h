@@ -105,6 +105,9 @@ typedef struct tfa_plan_info {
   uint64_t workspace_bytes;
   int32_t item_list;      /* 1 if the decode kernel takes its items from a list built on the
                              device for the call (longest first; one extra small kernel) */
+  int32_t pages;          /* 1 if the decode kernel works over whole pages (8 kv heads, 16-slot
+                             pages, one q token per sequence): an item is one sequence's split
+                             over all kv heads, so max_splits and num_items count per sequence */
 } tfa_plan_info;
 
 /* Fills *info for the call described by p on CUDA device `device` (device < 0: plan for

@@ -128,6 +128,42 @@ def test_wide_batch_decode(q_len):
     assert_parity(case)
 
 
+def _page_decode_case(hd, group, window=None, seed=41, n_seqs=10):
+    """One-token sequences with ragged lengths (every last page partial, one sequence of a
+    single token), 8 kv heads, 16-slot pages, NaN in every slot past a sequence's end."""
+    g = torch.Generator().manual_seed(seed)
+    k_lens = [int(x) for x in torch.randint(5000, 8192, (n_seqs,), generator=g)]
+    k_lens[3] = 1
+    k_lens = [k if k % 16 else k + 5 for k in k_lens]
+    case = reference_case([1] * n_seqs, k_lens, num_heads=8 * group, num_kv_heads=8, head_dim=hd, causal=True,
+                          window_size=window, block_size=16, seed=seed, name=f"pages_d{hd}_g{group}")
+    for b, n in enumerate(k_lens):
+        last = int(case.block_table[b, (n - 1) // 16])
+        case.k_cache[last, n % 16:] = float("nan")
+        case.v_cache[last, n % 16:] = float("nan")
+    return case
+
+
+@pytest.mark.parametrize("hd, group", [(64, 1), (64, 2), (64, 4), (128, 1), (128, 2), (128, 4)])
+def test_page_decode_kernel(hd, group):
+    """Large one-token decode calls with 8 kv heads and 16-slot pages run the page kernel
+    (one item = a sequence's split over all kv heads, one box per page)."""
+    case = _page_decode_case(hd, group)
+    c = case.to("cuda")
+    p = faf.plan(c.q, c.k_cache, c.v_cache, c.cu_seqlens_q, c.seqused_k, c.block_table, 1, c.max_seqlen_k, True)
+    assert p["pages"] == 1 and p["max_splits"] > 1
+    assert_parity(case)
+
+
+def test_page_decode_kernel_window():
+    case = _page_decode_case(128, 4, window=(6000, 0), seed=43, n_seqs=16)
+    c = case.to("cuda")
+    p = faf.plan(c.q, c.k_cache, c.v_cache, c.cu_seqlens_q, c.seqused_k, c.block_table, 1, c.max_seqlen_k, True,
+                 (6000, 0))
+    assert p["pages"] == 1
+    assert_parity(case)
+
+
 def test_c5_full_size_sample_vs_oracle():
     """The headline call at full size: all 256 sequences, the 2^21-block pool (137 GB of
     K/V), one call. The 16 longest and 16 seeded-random sequences are checked against the

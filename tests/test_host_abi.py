@@ -161,13 +161,15 @@ def test_reference_mode_matches_oracle_on_cpu(monkeypatch):
     torch.testing.assert_close(out, ref, atol=1e-5, rtol=1e-5)
 
 
-@pytest.mark.parametrize("kv_heads, q_heads, splits, cap", [
-    (8, 32, 4, 64),  # C5 on one GPU: ~2 items per SM of the max-length bound already
-    (1, 4, 10, 28),  # C5 shard of one kv head per GPU (8 GPUs): finer splits for the tail
+@pytest.mark.parametrize("kv_heads, q_heads, splits, cap, pages", [
+    (8, 32, 32, 8, 1),  # C5 on one GPU: page decode, items of 8 tiles x 8 kv heads
+    (1, 4, 10, 28, 0),  # C5 shard of one kv head per GPU (8 GPUs): finer splits for the tail
 ])
-def test_plan_split_rule_large_decode(kv_heads, q_heads, splits, cap):
+def test_plan_split_rule_large_decode(kv_heads, q_heads, splits, cap, pages):
     """Large decode calls get items of at least 16 tiles and ~16 items per SM of the
-    max-length work bound; the split count never exceeds what the longest sequence needs."""
+    max-length work bound (per kv head; the page kernel's items carry all 8 kv heads of a
+    sequence, so its cap is that divided by 8); the split count never exceeds what the
+    longest sequence needs."""
     p, _buf = _params(batch=256, total_q=256, num_q_heads=q_heads, num_kv_heads=kv_heads, head_dim=128,
                       max_seqlen_q=1, max_seqlen_k=32768, causal=1)
     p.q_stride[:] = [q_heads * 128, 128, 1]
@@ -177,13 +179,14 @@ def test_plan_split_rule_large_decode(kv_heads, q_heads, splits, cap):
     p.num_blocks, p.block_table_stride0 = 1 << 21, 2048
     info = _lib.TfaPlanInfo()
     assert _lib.load().tfa_plan(ctypes.byref(p), -1, ctypes.byref(info)) == 0
-    assert info.kernel == 0 and info.grid == 148
+    assert info.kernel == 0 and info.grid == 148 and info.pages == pages
     assert (info.max_splits, info.split_cap) == (splits, cap)
 
 
 def test_plan_small_decode_keeps_coarse_splits():
     """C4-sized calls: 128 (sequence, kv head) groups already fill one wave of 148 SMs, so
-    the latency-bound rule drops the split (a second wave and the combine cost more)."""
+    the latency-bound rule drops the split (a second wave and the combine cost more), and
+    the per-head kernel runs (the page kernel would need splits to fill the grid)."""
     p, _buf = _params(batch=16, total_q=16, num_q_heads=32, num_kv_heads=8, head_dim=64,
                       max_seqlen_q=1, max_seqlen_k=8192, causal=1, window_left=1024, window_right=0)
     p.q_stride[:] = [32 * 64, 64, 1]
@@ -193,7 +196,7 @@ def test_plan_small_decode_keeps_coarse_splits():
     p.num_blocks, p.block_table_stride0 = 8192, 512
     info = _lib.TfaPlanInfo()
     assert _lib.load().tfa_plan(ctypes.byref(p), -1, ctypes.byref(info)) == 0
-    assert info.kernel == 0 and info.max_splits == 1 and info.combine == 0
+    assert info.kernel == 0 and info.pages == 0 and info.max_splits == 1 and info.combine == 0
 
 
 @pytest.mark.parametrize("batch, heads, kv_heads, max_q, kernel", [
