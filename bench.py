@@ -38,8 +38,9 @@ METRIC = "decode attn KV-read HBM TB/s (C5 large-batch decode)"
 UNIT = "TB/s"
 L2_BYTES = 126 * 1024 * 1024
 # DRAM bytes (read + write) of one decode_kernel launch per algorithmic K/V byte, from an
-# ncu capture of the decode kernel on a reduced C5 (traffic grows with the K/V bytes read).
-TRAFFIC_PER_KV_BYTE = (471.91e6 + 4.19e6) / 471.49e6
+# ncu captures on a reduced C5 (traffic grows with the K/V bytes read): the page decode
+# kernel (one GPU: 8 kv heads) and the per-head decode kernel (kv-head shards)
+TRAFFIC_PER_KV_BYTE = {True: (471.88e6 + 5.79e6) / 471.49e6, False: (471.91e6 + 4.19e6) / 471.49e6}
 
 
 def parse_args():
@@ -470,7 +471,7 @@ def side_configs(pk: dict) -> dict:
         us = time_graph_marginal(case) if not name.startswith("P") else us_iso
         p = plan_of(case)
         entry = {"us_per_call": round(us, 2), "us_per_call_isolated": round(us_iso, 2),
-                 "kernel": "decode" if p["kernel"] == 0 else "prefill",
+                 "kernel": ("decode pages" if p.get("pages") else "decode") if p["kernel"] == 0 else "prefill",
                  "splits": p["max_splits"], "tokens_per_s": round(case.q.shape[0] / (us * 1e-6), 1),
                  "timing": ("marginal cost per call in a stream of calls, each after an L2 flush (graph of "
                             "[flush, call] x 20 minus graph of [flush] x 20); us_per_call_isolated = CUDA events "
@@ -717,9 +718,10 @@ def run_ours(args):
             "kv_bytes_per_step": kvb_total,
             "tokens_per_s": case.q.shape[0] / (ms * 1e-3),
             "roofline": {
-                "kernel": "decode_kernel (tfa_decode.cu)", "bound": "hbm", "achieved": achieved_gbs,
+                "kernel": ("decode_page_kernel (tfa_decode_pages.cu)" if p.get("pages")
+                           else "decode_kernel (tfa_decode.cu)"), "bound": "hbm", "achieved": achieved_gbs,
                 "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved_gbs / pk["hbm_gbs"],
-                "peak_source": pk["source"], "traffic": kvb_local * TRAFFIC_PER_KV_BYTE,
+                "peak_source": pk["source"], "traffic": kvb_local * TRAFFIC_PER_KV_BYTE[bool(p.get("pages"))],
                 "traffic_unit": "bytes per launch (ncu, scaled from reduced C5)",
                 "note": "achieved = algorithmic K/V bytes per launch / mean CUDA-event duration of the attention "
                         "kernel alone (tfa_fwd_timed), max over ranks",

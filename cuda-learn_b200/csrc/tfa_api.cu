@@ -153,11 +153,12 @@ int make_plan_one(const tfa_fwd_params* p, int device, Plan* pl) {
   // Large decode calls over whole pages (8 kv heads x 16 slots = one 128-row tile per page,
   // one q token per sequence): an item carries all kv heads of a sequence's split, so
   // splits are counted per sequence and the per-head kernel's cap is divided by the kv
-  // heads (about the same bytes per item). It reads each page as one contiguous box and
-  // issues a quarter of the exponentials per byte; on C5 (one B200) it matches the per-head
-  // kernel in a short burst and streams 1.8 % faster over a second of calls under the
-  // power cap. Latency-bound calls stay on the per-head kernel, which needs no split
-  // (C4: 24 vs 34 us per call on the page kernel with splits and the combine).
+  // heads (about the same bytes per item; items twice or four times as large measured
+  // slower). It reads each page as one contiguous box and issues a quarter of the
+  // exponentials per byte; on C5 (one B200, calls back to back as in a serving loop) it
+  // streams 2-4 % faster than the per-head kernel. Latency-bound calls stay on the per-head
+  // kernel, which needs no split (C4: 24 vs 34 us per call on the page kernel with splits
+  // and the combine).
   pl->pages = (TFA_PAGE_DECODE && decode && p->max_seqlen_q == 1 && p->num_splits == 0 &&
                est_all >= 32 * (int64_t)sms &&
                page_decode_supported((int)p->head_dim, (int)p->num_kv_heads, (int)p->block_size, (int)G))
