@@ -409,19 +409,21 @@ def _item_list_case():
                           seed=31)
 
 
-@pytest.mark.parametrize("name", ["C2", "C1", "list"], ids=["decode_split", "prefill", "decode_item_list"])
+@pytest.mark.parametrize("name", ["C2", "C1", "list", "pages"],
+                         ids=["decode_split", "prefill", "decode_item_list", "decode_pages"])
 def test_time_limit_reports_error_and_recovers(monkeypatch, name):
     """Every in-kernel wait is bounded. The test hook makes each CTA wait on a barrier
     nothing arrives on: after the wait's limit (about 1 s) the call must record a time-limit
     error (101-103: whichever warp's wait expired first), every warp must unwind (no hang,
     no fault), the error word must clear, and the next call on the same stream and workspace
     must be correct."""
-    case = _item_list_case() if name == "list" else baseline_config(name)
+    case = (_item_list_case() if name == "list" else _page_decode_case(128, 4) if name == "pages"
+            else baseline_config(name))
     c = case.to("cuda")
-    if name == "list":
+    if name in ("list", "pages"):
         p = faf.plan(c.q, c.k_cache, c.v_cache, c.cu_seqlens_q, c.seqused_k, c.block_table, c.max_seqlen_q,
                      c.max_seqlen_k, True)
-        assert p["item_list"] == 1
+        assert p["item_list" if name == "list" else "pages"] == 1
     out = torch.empty_like(c.q)
     monkeypatch.setenv("TFA_DEBUG_STALL_WAIT", "1")
     faf.flash_attn_varlen_func(**c.kwargs(), out=out)
