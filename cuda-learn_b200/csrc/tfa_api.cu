@@ -90,7 +90,7 @@ struct Plan {
   size_t ws_bytes;
 };
 
-int make_plan_one(const tfa_fwd_params* p, int device, Plan* pl) {
+int make_plan_one(const tfa_fwd_params* p, int device, Plan* pl, bool allow_pages = true) {
   const int64_t G = p->num_q_heads / p->num_kv_heads;
   const bool decode = p->max_seqlen_q * G <= 16;
   pl->kernel = decode ? 0 : 1;
@@ -159,7 +159,7 @@ int make_plan_one(const tfa_fwd_params* p, int device, Plan* pl) {
   // streams 2-4 % faster than the per-head kernel. Latency-bound calls stay on the per-head
   // kernel, which needs no split (C4: 24 vs 34 us per call on the page kernel with splits
   // and the combine).
-  pl->pages = (TFA_PAGE_DECODE && decode && p->max_seqlen_q == 1 && p->num_splits == 0 &&
+  pl->pages = (TFA_PAGE_DECODE && allow_pages && decode && p->max_seqlen_q == 1 && p->num_splits == 0 &&
                est_all >= 32 * (int64_t)sms &&
                page_decode_supported((int)p->head_dim, (int)p->num_kv_heads, (int)p->block_size, (int)G))
                   ? 1
@@ -236,8 +236,10 @@ struct FullPlan {
   size_t zero_off[2], zero_bytes[2];
 };
 
-int make_plan(const tfa_fwd_params* p, int device, FullPlan* fp) {
-  int rc = make_plan_one(p, device, &fp->pre);
+// allow_pages = false plans every decode call for the per-head kernel (the allocation-free
+// entry point: the page kernel's split partials can exceed its fixed workspace).
+int make_plan(const tfa_fwd_params* p, int device, FullPlan* fp, bool allow_pages = true) {
+  int rc = make_plan_one(p, device, &fp->pre, allow_pages);
   if (rc != TFA_OK) return rc;
   const int64_t G = p->num_q_heads / p->num_kv_heads;
   fp->mixed = (fp->pre.kernel == 1 && p->batch >= kMixedMinBatch && G <= 16) ? 1 : 0;
@@ -354,6 +356,7 @@ constexpr size_t kKeyBytes = offsetof(tfa_fwd_params, num_splits) + sizeof(int32
 struct CachedCall {
   unsigned char key[kKeyBytes];
   int dev;
+  bool allow_pages;
   bool valid;
   FullPlan fp;
   KvMaps maps;
@@ -363,10 +366,10 @@ constexpr int kCachedCalls = 8;
 thread_local CachedCall t_calls[kCachedCalls];
 thread_local unsigned t_next_call = 0;
 
-const CachedCall* find_call(const tfa_fwd_params* a, int dev) {
+const CachedCall* find_call(const tfa_fwd_params* a, int dev, bool allow_pages = true) {
   for (int i = 0; i < kCachedCalls; ++i) {
     const CachedCall& c = t_calls[i];
-    if (c.valid && c.dev == dev && std::memcmp(c.key, a, kKeyBytes) == 0) return &c;
+    if (c.valid && c.dev == dev && c.allow_pages == allow_pages && std::memcmp(c.key, a, kKeyBytes) == 0) return &c;
   }
   return nullptr;
 }
@@ -436,11 +439,13 @@ size_t tfa_workspace_size(const tfa_fwd_params* p, int device) {
 
 namespace tfa {
 
-int workspace_zero_ranges(const tfa_fwd_params* p, int device, size_t off[2], size_t bytes[2]) {
+int workspace_zero_ranges(const tfa_fwd_params* p, int device, size_t off[2], size_t bytes[2], bool allow_pages,
+                          size_t* ws_bytes) {
   int rc = validate(p);
   if (rc != TFA_OK) return rc;
   FullPlan fp;
-  if ((rc = make_plan(p, device, &fp)) != TFA_OK) return rc;
+  if ((rc = make_plan(p, device, &fp, allow_pages)) != TFA_OK) return rc;
+  if (ws_bytes) *ws_bytes = fp.ws_bytes;
   for (int i = 0; i < 2; ++i) {
     off[i] = fp.zero_off[i];
     bytes[i] = fp.zero_bytes[i];
@@ -450,12 +455,12 @@ int workspace_zero_ranges(const tfa_fwd_params* p, int device, size_t off[2], si
 
 // Shared by every forward entry point: checks, plan, descriptors, launches.
 int fwd_impl(const tfa_fwd_params* a, void* workspace, size_t workspace_bytes, void* stream, void* ev_begin,
-             void* ev_end) {
+             void* ev_end, bool allow_pages) {
   if (!a) return TFA_ERR_NULL_POINTER;
   int rc = TFA_OK;
   int dev = 0;
   const bool have_dev = current_device(&dev) == TFA_OK;
-  const CachedCall* hit = have_dev ? find_call(a, dev) : nullptr;
+  const CachedCall* hit = have_dev ? find_call(a, dev, allow_pages) : nullptr;
   if (!hit) {
     if ((rc = validate(a)) != TFA_OK) return rc;  // argument errors first, as before any CUDA call
     if (a->batch == 0 || a->total_q == 0) return TFA_OK;
@@ -463,7 +468,7 @@ int fwd_impl(const tfa_fwd_params* a, void* workspace, size_t workspace_bytes, v
     if ((rc = check_device(dev)) != TFA_OK) return rc;
     CachedCall& c = t_calls[t_next_call++ % kCachedCalls];
     c.valid = false;
-    if ((rc = make_plan(a, dev, &c.fp)) != TFA_OK) return rc;
+    if ((rc = make_plan(a, dev, &c.fp, allow_pages)) != TFA_OK) return rc;
     const int box_rows = a->block_size < 16 ? (int)a->block_size : 16;
     if ((rc = encode_maps(a, box_rows, c.fp.pre.pages != 0, &c.maps)) != TFA_OK) return rc;
     std::memset(&c.q_map, 0, sizeof(c.q_map));
@@ -481,6 +486,7 @@ int fwd_impl(const tfa_fwd_params* a, void* workspace, size_t workspace_bytes, v
     }
     std::memcpy(c.key, a, kKeyBytes);
     c.dev = dev;
+    c.allow_pages = allow_pages;
     c.valid = true;
     hit = &c;
   }
@@ -553,13 +559,13 @@ int fwd_impl(const tfa_fwd_params* a, void* workspace, size_t workspace_bytes, v
 extern "C" {
 
 int tfa_fwd(const tfa_fwd_params* a, void* workspace, size_t workspace_bytes, void* stream) {
-  return fwd_impl(a, workspace, workspace_bytes, stream, nullptr, nullptr);
+  return fwd_impl(a, workspace, workspace_bytes, stream, nullptr, nullptr, true);
 }
 
 int tfa_fwd_timed(const tfa_fwd_params* a, void* workspace, size_t workspace_bytes, void* stream, void* main_begin,
                   void* main_end) {
   if (!main_begin || !main_end) return TFA_ERR_NULL_POINTER;
-  return fwd_impl(a, workspace, workspace_bytes, stream, main_begin, main_end);
+  return fwd_impl(a, workspace, workspace_bytes, stream, main_begin, main_end, true);
 }
 
 int tfa_read_device_error(void* workspace, void* stream, int* err) {

@@ -64,22 +64,22 @@ extern "C" int tfa_fwd_static_workspace(const tfa_fwd_params* p, void* stream) {
   if (p->batch == 0 || p->total_q == 0) return tfa_fwd(p, nullptr, 0, stream);  // validates, launches nothing
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return TFA_ERR_CUDA;
-  const size_t need = tfa_workspace_size(p, dev);
-  if (need == 0) return tfa_fwd(p, nullptr, 0, stream);  // invalid arguments: same status as tfa_fwd
+  // Planned for the per-head decode kernel only: the page kernel's split partials can
+  // exceed the fixed workspace. The scheduler counters, the error word and the decode
+  // kernel's per-group split counters must start at zero; the split partials are fully
+  // written before they are read, so only those leading ranges are cleared.
+  size_t off[2], bytes[2], need = 0;
+  if (workspace_zero_ranges(p, dev, off, bytes, false, &need) != TFA_OK)
+    return tfa_fwd(p, nullptr, 0, stream);  // invalid arguments: same status as tfa_fwd
   if (need > (size_t)TFA_STATIC_WORKSPACE_BYTES) return TFA_ERR_STATIC_WORKSPACE_LIMIT;
   void* ws = nullptr;
   int rc = static_workspace_for_current_device(&ws);
   if (rc != TFA_OK) return rc;
-  // The scheduler counters, the error word and the decode kernel's per-group split
-  // counters must start at zero; the split partials are fully written before they are
-  // read, so only those leading ranges are cleared.
-  size_t off[2], bytes[2];
-  if ((rc = workspace_zero_ranges(p, dev, off, bytes)) != TFA_OK) return rc;
   for (int i = 0; i < 2; ++i)
     if (bytes[i] && cudaMemsetAsync(static_cast<unsigned char*>(ws) + off[i], 0, bytes[i],
                                     reinterpret_cast<cudaStream_t>(stream)) != cudaSuccess)
       return TFA_ERR_CUDA;
-  return fwd_impl(p, ws, TFA_STATIC_WORKSPACE_BYTES, stream, nullptr, nullptr);
+  return fwd_impl(p, ws, TFA_STATIC_WORKSPACE_BYTES, stream, nullptr, nullptr, false);
 }
 
 extern "C" int tfa_read_static_workspace_error(void* stream, int* err) {

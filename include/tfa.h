@@ -139,8 +139,11 @@ TFA_API int tfa_fwd_timed(const tfa_fwd_params* p, void* workspace, size_t works
  * but has no device allocator to create the workspace tfa_fwd needs. Same arguments,
  * checks and results as tfa_fwd, but the split-KV workspace is a TFA_STATIC_WORKSPACE_BYTES
  * array in the library's own device memory (present on every GPU where the library is
- * loaded, until exit); nothing is allocated. Calls needing a larger workspace
- * (tfa_workspace_size) return TFA_ERR_STATIC_WORKSPACE_LIMIT. All calls on a device share
+ * loaded, until exit); nothing is allocated. Decode calls are planned for the per-head
+ * decode kernel (the page decode kernel's split partials can exceed the array), so the
+ * plan and the workspace it needs may differ from tfa_plan / tfa_workspace_size; calls
+ * whose plan still needs more than the array return TFA_ERR_STATIC_WORKSPACE_LIMIT (a
+ * call with num_splits forced, for example). All calls on a device share
  * the array, so calls that can overlap on the GPU race and must not be issued. The first
  * call on a device looks up the array's address with that device current and should come
  * before any stream capture. Kernel errors of these calls land in the array's error word,

@@ -51,6 +51,16 @@ def _item_list_case():
                           seed=31)
 
 
+def _large_page_case():
+    """One-token decode, 8 kv heads, 16-slot pages, a 32768-token bound: the caller-workspace
+    entry point runs the page kernel with ~37 splits per sequence (> 32 MiB of partials)."""
+    g = torch.Generator().manual_seed(53)
+    k_lens = [int(x) for x in torch.randint(100, 2000, (64,), generator=g)]
+    k_lens[5] = 32768
+    return reference_case([1] * 64, k_lens, num_heads=32, num_kv_heads=8, head_dim=128, causal=True,
+                          block_size=16, seed=53)
+
+
 def _static_call(c, num_splits=0):
     out = torch.full_like(c.q, float("nan"))
     lse = torch.full((c.q.shape[0], c.q.shape[1]), float("nan"), dtype=torch.float32, device=c.q.device)
@@ -74,8 +84,9 @@ def _static_call(c, num_splits=0):
         (lambda: reference_case([1, 1, 1, 40, 1, 1, 1, 2], [900, 700, 1200, 300, 129, 800, 60, 90], num_heads=8,
                                 num_kv_heads=2, head_dim=64, causal=True, block_size=16, seed=8), 0),
                                                              # both kernels in one call (chunked prefill)
+        (_large_page_case, 0),                               # planned per head here (page plan too large)
     ],
-    ids=["C2", "C3_split3", "C4_b8", "hd128_mixed", "item_list", "mixed_dispatch"],
+    ids=["C2", "C3_split3", "C4_b8", "hd128_mixed", "item_list", "mixed_dispatch", "large_pages_plan"],
 )
 def test_static_workspace_matches_tfa_fwd_twice(make, splits):
     case = make()
@@ -95,6 +106,20 @@ def test_static_workspace_matches_tfa_fwd_twice(make, splits):
             fin = torch.isfinite(want_lse)
             assert torch.equal(fin, torch.isfinite(lse))
             assert (lse[fin] - want_lse[fin]).abs().max().item() <= LSE_TOL
+
+
+def test_static_workspace_keeps_large_decode_on_the_per_head_plan():
+    """The page decode kernel's split partials of this call exceed the static array, so the
+    allocation-free entry point plans it for the per-head kernel, which fits (the call itself
+    is checked against tfa_fwd and the oracle by the parametrized test above)."""
+    c = _large_page_case().to("cuda")
+    out = torch.empty_like(c.q)
+    p = _params(c, out, None)
+    info = _lib.TfaPlanInfo()
+    assert _lib.load().tfa_plan(ctypes.byref(p), torch.cuda.current_device(), ctypes.byref(info)) == 0
+    assert info.pages == 1 and info.workspace_bytes > STATIC_WS_BYTES
+    _static_call(c)
+    assert _static_error() == 0
 
 
 def test_static_workspace_reports_bad_block_id():
