@@ -137,6 +137,7 @@ __global__ void __launch_bounds__(224, 1)
   __shared__ uint64_t s_full[2], s_free[2], p_full[2], o_full[2], o_free[2];
   __shared__ uint64_t item_full[2], item_empty[2], q_full[2], red_bar;
   __shared__ int item_slot[2];
+  __shared__ PageWork item_work[2];  // the item's descriptor, published by the K producer
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_flag;
   __shared__ uint64_t stall_bar;  // never arrived on: the time-limit test hook waits here
@@ -218,6 +219,7 @@ __global__ void __launch_bounds__(224, 1)
         if (lane == 0) {
           item_slot[slot] = idx < p.num_items ? idx : p.num_items;
           if (idx < p.num_items) {
+            item_work[slot] = pw;
             mbar_arrive_expect_tx(&q_full[slot], (uint32_t)Cfg::kQBytes);
             const uint32_t qdst = smem_u32(q_smem + slot * Cfg::kQBytes);
 #pragma unroll
@@ -248,7 +250,7 @@ __global__ void __launch_bounds__(224, 1)
         if (!mbar_wait(&item_full[slot], (k >> 1) & 1, &abort_flag, p.err, kDevErrTimeoutProducer)) break;
         idx = item_slot[slot];
         if (idx >= p.num_items) break;
-        const PageWork pw = page_work(p, idx);
+        const PageWork pw = item_work[slot];
         for (int pg = pw.pg_begin; pg < pw.pg_end; ++pg, ++c) {
           const int st = c % stages;
           if (!mbar_wait(&empty[st], ((c / stages) & 1) ^ 1, &abort_flag, p.err, kDevErrTimeoutProducer)) goto done;
@@ -272,7 +274,7 @@ __global__ void __launch_bounds__(224, 1)
       if (!mbar_wait(&item_full[slot], (k >> 1) & 1, &abort_flag, p.err, kDevErrTimeoutMma)) break;
       const int idx = item_slot[slot];
       if (idx >= p.num_items) break;
-      const PageWork pw = page_work(p, idx);
+      const PageWork pw = item_work[slot];
       if (p.debug_stall && k == 0 && !mbar_wait(&stall_bar, 0, &abort_flag, p.err, kDevErrTimeoutMma)) break;
       const int n = pw.pg_end - pw.pg_begin;
       const uint32_t q_addr = smem_u32(q_smem + slot * Cfg::kQBytes);
@@ -381,7 +383,7 @@ __global__ void __launch_bounds__(224, 1)
       if (!mbar_wait(&item_full[slot], (k >> 1) & 1, &abort_flag, p.err, kDevErrTimeoutSoftmax)) break;
       const int idx = item_slot[slot];
       if (idx >= p.num_items) break;
-      const PageWork pw = page_work(p, idx);
+      const PageWork pw = item_work[slot];
       const int n = pw.pg_end - pw.pg_begin;
       const int tok = pw.w.q0;
       float m[G], l[G], a_prev[N], o[N];
