@@ -25,7 +25,7 @@ constexpr size_t kCtrlBytes = 256;  // workspace control block: sched[2], err, d
 constexpr size_t kCounterRegionEnd = 64 * 1024;
 constexpr int64_t kMaxCountedGroups = (int64_t)((kCounterRegionEnd - kCtrlBytes) / sizeof(int));
 constexpr int kMaxDevices = 128;
-#ifndef TFA_PAGE_DECODE
+#ifndef TFA_PAGE_DECODE  // build switch: 0 keeps every decode call on the per-head kernel
 #define TFA_PAGE_DECODE 1
 #endif
 
@@ -251,9 +251,9 @@ int make_plan(const tfa_fwd_params* p, int device, FullPlan* fp, bool allow_page
   if (fp->mixed) {
     tfa_fwd_params d = *p;
     d.max_seqlen_q = 16 / G;  // the decode kernel's sequences are at most this long
-    if ((rc = make_plan_one(&d, device, &fp->dec)) != TFA_OK) return rc;
+    // the decode part runs the per-head kernel (its sequences may hold several tokens)
+    if ((rc = make_plan_one(&d, device, &fp->dec, false)) != TFA_OK) return rc;
     fp->dec.item_list = 0;  // the decode part of a mixed call keeps slot order
-    fp->dec.pages = 0;
     if (fp->dec.ws_bytes > fp->dec.list_off && fp->dec.list_off) fp->dec.ws_bytes = fp->dec.list_off;
     // the decode part counts its groups in the call's own counter region, so the call
     // reserves it whenever the decode part has splits
