@@ -218,3 +218,39 @@ def test_plan_mixed_dispatch(batch, heads, kv_heads, max_q, kernel):
     assert lib.tfa_plan(ctypes.byref(p), -1, ctypes.byref(info)) == 0
     assert info.kernel == kernel
     assert lib.tfa_workspace_size(ctypes.byref(p), -1) == info.workspace_bytes
+
+
+def _decode_params(batch=256, hq=32, hkv=8, hd=128, bs=16, max_q=1, max_k=32768, num_splits=0):
+    p, buf = _params(batch=batch, total_q=batch * max_q, num_q_heads=hq, num_kv_heads=hkv, head_dim=hd,
+                     block_size=bs, max_seqlen_q=max_q, max_seqlen_k=max_k, causal=1)
+    p.q_stride[:] = [hq * hd, hd, 1]
+    p.out_stride[:] = [hq * hd, hd, 1]
+    p.k_stride[:] = [bs * hkv * hd, hkv * hd, hd, 1]
+    p.v_stride[:] = [bs * hkv * hd, hkv * hd, hd, 1]
+    p.num_blocks, p.block_table_stride0 = 1 << 21, (max_k + bs - 1) // bs
+    p.num_splits = num_splits
+    return p, buf
+
+
+@pytest.mark.parametrize("over, pages", [
+    (dict(), 1),                          # C5: 8 kv heads, 16-slot pages, one token, a large call
+    (dict(hd=64), 1),
+    (dict(hq=8), 1),                      # GQA group 1
+    (dict(hkv=4, hq=16), 0),              # 4 kv heads: a page is 64 rows
+    (dict(bs=32), 0),                     # 32-slot pages
+    (dict(max_q=2), 0),                   # two tokens per sequence
+    (dict(hq=64, hd=64), 0),              # GQA group 8
+    (dict(num_splits=4), 0),              # forced split count
+    (dict(batch=2, max_k=4096), 0),       # latency-bound
+])
+def test_plan_page_decode_selection(over, pages):
+    """The page decode kernel is planned only for large one-token decode calls with 8 kv
+    heads, 16-slot pages and a GQA group of 1, 2 or 4; its items count per sequence."""
+    p, _buf = _decode_params(**over)
+    info = _lib.TfaPlanInfo()
+    assert _lib.load().tfa_plan(ctypes.byref(p), -1, ctypes.byref(info)) == 0
+    assert info.kernel == 0 and info.pages == pages
+    per_group = p.batch * (1 if pages else p.num_kv_heads)
+    assert info.num_items == info.max_splits * per_group
+    if pages:
+        assert info.combine == 1 and info.item_list == 0
