@@ -254,3 +254,15 @@ def test_plan_page_decode_selection(over, pages):
     assert info.num_items == info.max_splits * per_group
     if pages:
         assert info.combine == 1 and info.item_list == 0
+
+
+def test_plan_info_mirror_covers_the_c_struct():
+    """tfa_plan writes nothing past the ctypes mirror of tfa_plan_info (a field added to the
+    C struct but not to the mirror would overwrite the caller's memory)."""
+    size = ctypes.sizeof(_lib.TfaPlanInfo)
+    buf = (ctypes.c_ubyte * (size + 64))(*([0xA5] * (size + 64)))
+    p, _b = _decode_params()
+    info = _lib.TfaPlanInfo.from_buffer(buf)
+    assert _lib.load().tfa_plan(ctypes.byref(p), -1, ctypes.byref(info)) == 0
+    assert bytes(buf[size:]) == bytes([0xA5] * 64)
+    assert info.pages == 1 and info.workspace_bytes > 0
