@@ -8,8 +8,8 @@ With N GPUs (one process per GPU, torchrun) the kv heads are sharded: each rank 
 8/N kv heads (and their q heads) of every sequence in its own pool; no collective runs in
 the timed region. Total work is fixed, so scaling is "strong".
 
-Per step: one forward call over the whole batch. Inputs are larger than L2 (about
-9.6 GB of K/V per step), so no L2 flush is needed for the headline. C1-C4 (N=1 only)
+Per step: one forward call over the whole batch. Inputs are larger than L2 (8.60 GB of
+K/V per step at one GPU), so no L2 flush is needed for the headline. C1-C4 (N=1 only)
 are timed one call at a time from a CUDA graph with a 256 MB L2 flush between calls.
 
 ``--impl reference`` times the reference's own CPU algorithm (the oracle port of
@@ -37,7 +37,7 @@ import torch  # noqa: E402
 METRIC = "decode attn KV-read HBM TB/s (C5 large-batch decode)"
 UNIT = "TB/s"
 L2_BYTES = 126 * 1024 * 1024
-# DRAM bytes (read + write) of one decode_kernel launch per algorithmic K/V byte, from an
+# DRAM bytes (read + write) of one attention-kernel launch per algorithmic K/V byte, from
 # ncu captures on a reduced C5 (traffic grows with the K/V bytes read): the page decode
 # kernel (one GPU: 8 kv heads) and the per-head decode kernel (kv-head shards)
 TRAFFIC_PER_KV_BYTE = {True: (471.88e6 + 5.79e6) / 471.49e6, False: (471.91e6 + 4.19e6) / 471.49e6}
